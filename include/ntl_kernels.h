@@ -1,0 +1,118 @@
+/*
+ * ntl_kernels.h — C ABI of libntl_kernels.so, the sm_100a kernel library behind the
+ * ntilang-compatible Python surface.
+ *
+ * In the reference, every compiled kernel is reached through one boundary:
+ * CompiledKernel.__call__ (python/ntilang/compiler.py:134-200) validates torch tensors and
+ * calls `executable(*ffi_arguments)` (compiler.py:197), a TVM-FFI function that
+ * `cute.compile(..., "--enable-tvm-ffi")` built from generated CuTe-DSL source
+ * (python/ntilang/codegen.py:2206-2259).  Each entry point below replaces that FFI call
+ * for one op family the reference's emitter produces; the Python side keeps the
+ * reference's argument checks and passes raw device pointers, sizes and the caller's
+ * CUDA stream (torch's current stream, which is what TVM-FFI's environment stream
+ * follows in the reference — pinned by tests/test_gpu.py:90-101).
+ *
+ * Conventions
+ *  - All pointers are device pointers owned by the caller; tensors are dense row-major.
+ *  - fp16 data is passed as `const uint16_t*` (IEEE binary16 bit patterns).
+ *  - `stream` is a cudaStream_t (NULL = legacy default stream).  Launches are
+ *    asynchronous; nothing here synchronises the stream or allocates device memory.
+ *  - Return 0 on success or an NTL_ERR_* code; ntl_last_error() then describes the
+ *    failure (thread-local).  Argument errors are detected on the host before launch.
+ */
+#ifndef NTL_KERNELS_H
+#define NTL_KERNELS_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef void* ntl_stream_t;
+
+enum {
+  NTL_OK = 0,
+  NTL_ERR_INVALID = 1,     /* bad size / null pointer / unsupported parameter */
+  NTL_ERR_UNSUPPORTED = 2, /* shape outside what the kernels implement */
+  NTL_ERR_CUDA = 3,        /* a CUDA runtime call or launch failed */
+  NTL_ERR_TIMEOUT = 4,     /* a bounded device-side wait gave up (see ntl_device_status) */
+  NTL_ERR_ALIGNMENT = 5    /* pointer alignment not met for the requested path */
+};
+
+/* Library version (major*10000 + minor*100 + patch). */
+int ntl_version(void);
+
+/* Message for the last non-zero return on this thread ("" if none). */
+const char* ntl_last_error(void);
+
+/* Vector add C[i] = A[i] + B[i] for i < n (fp32).  Replaces the FFI call of the
+ * elementwise kernel emitted for examples/vector_add.py:5-10 (codegen.py:1494-1517 store,
+ * :1694-1734 parallel loop).  Bit-exact: one IEEE fp32 add per element. */
+int ntl_vadd_f32(const float* a, const float* b, float* c, int64_t n, ntl_stream_t stream);
+
+/* Elementwise binary op over n fp32 elements: op 0 = add, 1 = sub, 2 = mul.  Same
+ * reference emitter as ntl_vadd_f32 (codegen.py:1494-1517, :1694-1734). */
+int ntl_binary_f32(int op, const float* a, const float* b, float* c, int64_t n, ntl_stream_t stream);
+
+/* Inclusive prefix sum along each row of a [rows, cols] fp32 matrix; reverse != 0 scans
+ * from the last column.  Replaces the FFI call of the warp scan emitted by
+ * python/ntilang/scan.py:132-240 for examples/cumsum.py:7-14.  The addition DAG is the
+ * reference's: 32-column Hillis-Steele segments (offsets 1,2,4,8,16) followed by a
+ * sequential carry carry_{s+1} = seg_s[last] + carry_s starting from +0
+ * (scan.py:168-237, evaluate :349-389), so results are bit-identical to it. */
+int ntl_cumsum_f32(const float* x, float* y, int64_t rows, int64_t cols, int reverse, ntl_stream_t stream);
+
+/* Row softmax y = exp(x - max) / sum(exp(x - max)) over [rows, cols] fp32.  Replaces the
+ * FFI call of the row-reduction kernel emitted for examples/softmax.py:9-25
+ * (codegen.py:1028-1240).  Sums follow the reference's balanced tree over the row padded
+ * to the next power of two (codegen.py:1094-1151). */
+int ntl_softmax_f32(const float* x, float* y, int64_t rows, int64_t cols, ntl_stream_t stream);
+
+/* RMSNorm y = (x * rsqrt(sum(x^2) * inv_n + eps)) * w over [rows, cols] fp32, w[cols].
+ * Replaces the FFI call of the kernel emitted for examples/rmsnorm.py:13-37; inv_n is the
+ * program's constant (the reference multiplies by 1/n, rmsnorm.py:10,34). */
+int ntl_rmsnorm_f32(const float* x, const float* w, float* y, int64_t rows, int64_t cols, float eps,
+                    float inv_n, ntl_stream_t stream);
+
+/* Bias modes of ntl_gemm_f16_f32. */
+enum { NTL_BIAS_NONE = 0, NTL_BIAS_N = 1, NTL_BIAS_MN = 2, NTL_BIAS_M = 3 };
+
+/* C[M,N] (fp32) = epilogue(A[M,K] @ B), fp16 operands, fp32 accumulation.
+ *   B is [K,N] row-major (b_trans = 0) or [N,K] row-major (b_trans = 1, T.gemm transpose_B).
+ *   epilogue: v = alpha * acc (+ bias[n] | bias[m,n] | bias[m]); if relu: v = max(v, 0).
+ * Replaces the FFI call of the GEMM emitted by codegen.py:969-1026 + :1611-1693 for
+ * examples/matmul.py:17-29 and its fused epilogue (codegen.py:1694-1734,
+ * examples/matmul_relu.py:31-38).  Aligned shapes (K, N multiples of 8; 16-byte aligned
+ * pointers) run the tcgen05/TMEM kernel; other shapes run a CUDA-core tiled kernel. */
+int ntl_gemm_f16_f32(const uint16_t* a, const uint16_t* b, float* c, const float* bias, int bias_mode,
+                     float alpha, int relu, int64_t M, int64_t N, int64_t K, int b_trans, ntl_stream_t stream);
+
+/* FlashAttention-2 forward, fp16 Q,K,V,O [batch, heads, seq, dim] row-major.
+ *   O = softmax_base2((Q K^T) * scale_log2 [causal: key <= query]) V, with P rounded to fp16
+ *   before the P V product and fp32 softmax statistics.
+ * Replaces the FFI call of the kernel emitted for examples/flash_attention.py:26-79
+ * (scale = log2(e)/sqrt(d) at :23, causal fill at :56-62, P cast at :74-75). */
+int ntl_fa2_fwd_f16(const uint16_t* q, const uint16_t* k, const uint16_t* v, uint16_t* o, int64_t batch,
+                    int64_t heads, int64_t seq, int64_t dim, float scale_log2, int causal, ntl_stream_t stream);
+
+/* Device status word of the bounded waits in the tcgen05 kernels on the current device:
+ * 0 = no timeout since the last clear, else a code naming the wait that gave up.  Reading
+ * it synchronises the device.  No reference counterpart (its kernels have no bounded
+ * waits); exposed so callers can turn a timed-out launch into an error. */
+int ntl_device_status(uint32_t* status_out);
+int ntl_clear_device_status(void);
+
+/* Spin limit of every bounded wait (default 1<<26 polls).  Test hook: a limit of 1 makes
+ * waits give up early so the timeout path can be exercised without hanging anything.
+ * No reference counterpart. */
+int ntl_set_wait_limit(int64_t polls);
+
+/* Number of kernel launches issued by this library in this process (all devices). */
+int64_t ntl_launch_count(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* NTL_KERNELS_H */

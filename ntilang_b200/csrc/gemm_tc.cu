@@ -1,0 +1,430 @@
+// FP16 GEMM with fp32 accumulation and a fused epilogue, sm_100a.
+//
+// Reference: the GEMM its emitter builds for examples/matmul.py:17-29 (codegen.py:969-1026
+// mma.sync m16n8k16 + ldmatrix, :1611-1693 cp.async pipeline, :1280-1316 raster swizzle)
+// and the fused epilogue of examples/matmul_relu.py:31-38 (codegen.py:1694-1734).
+//
+// Design (one CTA per SM, persistent):
+//   warp 0      TMA producer: A tile 128x64 (K-major) and B tile 64x256 (N-major, or K-major
+//               for transpose_B) into a 4-stage ring of 128B-swizzled smem stages.
+//   warp 1      allocates 512 TMEM columns (two 128x256 fp32 accumulators), one elected
+//               lane issues tcgen05.mma (M=128, N=256, K=16) and tcgen05.commit's the stage
+//               back to the producer / the accumulator to the epilogue.
+//   warps 2..5  epilogue: tcgen05.ld 32 lanes x 32 columns, alpha / bias / ReLU in registers,
+//               128-bit stores to C.  The double-buffered accumulator lets the epilogue of
+//               tile i overlap the main loop of tile i+1.
+// Every mbarrier wait is bounded (ntl_set_wait_limit); a wait that gives up records a
+// status code, raises the CTA abort flag, drains in-flight TMA loads and MMAs, frees TMEM
+// and returns.  Shapes TMA cannot address (K or N not a multiple of 8, unaligned pointers)
+// use a CUDA-core tiled kernel with the same epilogue.
+#include <atomic>
+#include <mutex>
+
+#include "ntl_common.cuh"
+
+namespace {
+
+constexpr int BM = 128, BN = 256, BK = 64, STAGES = 4;
+constexpr int A_STAGE = BM * BK * 2;        // 16 KB
+constexpr int B_STAGE = BN * BK * 2;        // 32 KB
+constexpr int STAGE_BYTES = A_STAGE + B_STAGE;
+constexpr int THREADS = 192;
+constexpr int TMEM_COLS = 512;
+constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*barriers*/ + 1024 /*alignment slack*/;
+constexpr int GROUP_M = 8;
+
+__device__ uint32_t g_gemm_status;
+
+struct GemmParams {
+  float* c;
+  const float* bias;
+  int bias_mode;
+  float alpha;
+  int relu;
+  int M, N, K;
+  int b_trans;
+  int vec_store;  // C rows 16-byte aligned
+  int64_t wait_limit;
+};
+
+struct __align__(8) SharedCtl {
+  uint64_t full[STAGES];
+  uint64_t empty[STAGES];
+  uint64_t acc_full[2];
+  uint64_t acc_empty[2];
+  uint64_t drain;
+  uint32_t tmem_base;
+  int abort;
+};
+
+__device__ __forceinline__ void tile_coords(int t, int num_m, int num_n, int& mb, int& nb) {
+  const int per_group = GROUP_M * num_n;
+  const int g = t / per_group;
+  const int first = g * GROUP_M;
+  const int size = min(num_m - first, GROUP_M);
+  const int r = t % per_group;
+  mb = first + r % size;
+  nb = r / size;
+}
+
+__device__ __forceinline__ void record_abort(SharedCtl* ctl, uint32_t code) {
+  atomicCAS(&g_gemm_status, 0u, code);
+  *reinterpret_cast<volatile int*>(&ctl->abort) = 1;
+}
+
+// v = acc * alpha + b as two rounded ops (the program's order), then optional ReLU.
+__device__ __forceinline__ float epi(float acc, float alpha, float b, int relu, int has_bias) {
+  float v = alpha == 1.0f ? acc : __fmul_rn(acc, alpha);
+  if (has_bias) v = __fadd_rn(v, b);
+  return relu ? fmaxf(v, 0.0f) : v;
+}
+
+__global__ void __launch_bounds__(THREADS, 1) gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_a,
+                                                             const __grid_constant__ CUtensorMap tmap_b,
+                                                             const GemmParams p) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + STAGES * A_STAGE;
+  SharedCtl* ctl = reinterpret_cast<SharedCtl*>(smem + STAGES * STAGE_BYTES);
+  volatile int* abort_flag = &ctl->abort;
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int num_m = (p.M + BM - 1) / BM;
+  const int num_n = (p.N + BN - 1) / BN;
+  const int num_tiles = num_m * num_n;
+  const int num_kb = (p.K + BK - 1) / BK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&ctl->full[s], 1);
+      mbar_init(&ctl->empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&ctl->acc_full[a], 1);
+      mbar_init(&ctl->acc_empty[a], 4);  // one arrival per epilogue warp
+    }
+    mbar_init(&ctl->drain, 1);
+    ctl->abort = 0;
+    fence_mbar_init();
+    prefetch_tensormap(&tmap_a);
+    prefetch_tensormap(&tmap_b);
+  }
+  if (warp == 1) {
+    tmem_alloc(&ctl->tmem_base, TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = ctl->tmem_base;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ TMA producer
+    if (elect_one_lane()) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int issued = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
+        int mb, nb;
+        tile_coords(t, num_m, num_n, mb, nb);
+        const int m0 = mb * BM, n0 = nb * BN;
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait_bounded(&ctl->empty[stage], phase ^ 1, p.wait_limit, abort_flag)) {
+            if (!*abort_flag) record_abort(ctl, NTL_STATUS_TMA_EMPTY_WAIT);
+            ok = false;
+            break;
+          }
+          uint8_t* a_dst = sA + stage * A_STAGE;
+          uint8_t* b_dst = sB + stage * B_STAGE;
+          mbar_arrive_expect_tx(&ctl->full[stage], STAGE_BYTES);
+          tma_load_2d(a_dst, &tmap_a, &ctl->full[stage], kb * BK, m0);
+          if (p.b_trans) {
+            tma_load_2d(b_dst, &tmap_b, &ctl->full[stage], kb * BK, n0);
+          } else {
+#pragma unroll
+            for (int i = 0; i < BN / 64; ++i)
+              tma_load_2d(b_dst + i * (64 * BK * 2), &tmap_b, &ctl->full[stage], n0 + i * 64, kb * BK);
+          }
+          ++issued;
+          if (++stage == STAGES) stage = 0, phase ^= 1;
+        }
+      }
+      if (!ok) {
+        // Drain: the last min(issued, STAGES) stages may still have loads in flight.
+        int s = stage;
+        uint32_t ph = phase;
+        for (int i = 0; i < STAGES && i < issued; ++i) {
+          if (--s < 0) s = STAGES - 1, ph ^= 1;
+          if (!mbar_wait_bounded(&ctl->full[s], ph, int64_t(1) << 24, nullptr))
+            atomicCAS(&g_gemm_status, 0u, NTL_STATUS_DRAIN_WAIT);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (elect_one_lane()) {
+      const uint32_t idesc = umma_idesc_f16_f32(BM, BN, 0, p.b_trans ? 0 : 1);
+      int stage = 0;
+      uint32_t phase = 0;
+      int local = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x, ++local) {
+        const int acc = local & 1;
+        const uint32_t acc_phase = (local >> 1) & 1;
+        if (!mbar_wait_bounded(&ctl->acc_empty[acc], acc_phase ^ 1, p.wait_limit, abort_flag)) {
+          if (!*abort_flag) record_abort(ctl, NTL_STATUS_ACC_EMPTY_WAIT);
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * BN;
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait_bounded(&ctl->full[stage], phase, p.wait_limit, abort_flag)) {
+            if (!*abort_flag) record_abort(ctl, NTL_STATUS_MMA_FULL_WAIT);
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(sA + stage * A_STAGE);
+          const uint32_t b_addr = smem_u32(sB + stage * B_STAGE);
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k) {
+            const uint64_t adesc = umma_desc_sw128(a_addr + k * 32, 16, 1024);
+            const uint64_t bdesc = p.b_trans ? umma_desc_sw128(b_addr + k * 32, 16, 1024)
+                                             : umma_desc_sw128(b_addr + k * 2048, 64 * BK * 2, 1024);
+            tc_mma_f16_ss(d_tmem, adesc, bdesc, idesc, (kb > 0 || k > 0) ? 1u : 0u);
+          }
+          tc_commit(&ctl->empty[stage]);
+          if (++stage == STAGES) stage = 0, phase ^= 1;
+        }
+        if (!ok) break;
+        tc_commit(&ctl->acc_full[acc]);
+      }
+      if (!ok) {
+        // Drain: wait until every MMA this thread issued has retired before TMEM is freed.
+        tc_commit(&ctl->drain);
+        if (!mbar_wait_bounded(&ctl->drain, 0, int64_t(1) << 24, nullptr))
+          atomicCAS(&g_gemm_status, 0u, NTL_STATUS_DRAIN_WAIT);
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue (warps 2..5)
+    const int quarter = warp & 3;  // TMEM lanes 32*quarter .. +31 are accessible to this warp
+    int local = 0;
+    for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++local) {
+      int mb, nb;
+      tile_coords(t, num_m, num_n, mb, nb);
+      const int acc = local & 1;
+      const uint32_t acc_phase = (local >> 1) & 1;
+      if (!mbar_wait_bounded(&ctl->acc_full[acc], acc_phase, p.wait_limit, abort_flag)) {
+        if (!*abort_flag) record_abort(ctl, NTL_STATUS_ACC_FULL_WAIT);
+        break;
+      }
+      __syncwarp();
+      tc_fence_after();
+      const int row = mb * BM + quarter * 32 + lane;
+      const bool row_ok = row < p.M;
+      float* crow = p.c + static_cast<int64_t>(row) * p.N;
+      const float row_bias = (p.bias_mode == NTL_BIAS_M && row_ok) ? __ldg(p.bias + row) : 0.0f;
+      for (int chunk = 0; chunk < BN / 32; ++chunk) {
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + acc * BN + chunk * 32, r);
+        tc_wait_ld();
+        const int col0 = nb * BN + chunk * 32;
+        if (!row_ok || col0 >= p.N) continue;
+        float v[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          float b = row_bias;
+          const int col = col0 + j;
+          if (p.bias_mode == NTL_BIAS_N) b = (col < p.N) ? __ldg(p.bias + col) : 0.0f;
+          else if (p.bias_mode == NTL_BIAS_MN) b = (col < p.N) ? __ldg(p.bias + static_cast<int64_t>(row) * p.N + col) : 0.0f;
+          v[j] = epi(__uint_as_float(r[j]), p.alpha, b, p.relu, p.bias_mode);
+        }
+        if (p.vec_store && col0 + 32 <= p.N) {
+#pragma unroll
+          for (int j = 0; j < 32; j += 4)
+            *reinterpret_cast<float4*>(crow + col0 + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+        } else {
+#pragma unroll
+          for (int j = 0; j < 32; ++j)
+            if (col0 + j < p.N) crow[col0 + j] = v[j];
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&ctl->acc_empty[acc]);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc(tmem_base, TMEM_COLS);
+}
+
+// ------------------------------------------------------------------ CUDA-core fallback
+// 64x64 output tile per 256-thread CTA, 4x4 outputs per thread, K step 16; fp16 operands
+// converted to fp32 in shared memory, fp32 FMA accumulation.  Used only for shapes the
+// TMA path cannot address.
+constexpr int FB_T = 64, FB_K = 16;
+
+__global__ void __launch_bounds__(256) gemm_simt_kernel(const __half* __restrict__ A, const __half* __restrict__ B,
+                                                        GemmParams p) {
+  __shared__ float As[FB_K][FB_T + 4];
+  __shared__ float Bs[FB_K][FB_T + 4];
+  const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
+  const int m0 = blockIdx.y * FB_T, n0 = blockIdx.x * FB_T;
+  float acc[4][4] = {};
+  for (int k0 = 0; k0 < p.K; k0 += FB_K) {
+    for (int i = threadIdx.x; i < FB_T * FB_K; i += 256) {
+      const int r = i / FB_K, kk = i % FB_K;
+      const int m = m0 + r, k = k0 + kk;
+      As[kk][r] = (m < p.M && k < p.K) ? __half2float(A[static_cast<int64_t>(m) * p.K + k]) : 0.0f;
+      const int n = n0 + r;
+      float bv = 0.0f;
+      if (n < p.N && k < p.K)
+        bv = __half2float(p.b_trans ? B[static_cast<int64_t>(n) * p.K + k] : B[static_cast<int64_t>(k) * p.N + n]);
+      Bs[kk][r] = bv;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int kk = 0; kk < FB_K; ++kk) {
+      float a[4], b[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) a[i] = As[kk][ty * 4 + i], b[i] = Bs[kk][tx * 4 + i];
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[i][j] = __fmaf_rn(a[i], b[j], acc[i][j]);
+    }
+    __syncthreads();
+  }
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int m = m0 + ty * 4 + i;
+    if (m >= p.M) continue;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int n = n0 + tx * 4 + j;
+      if (n >= p.N) continue;
+      float b = 0.0f;
+      if (p.bias_mode == NTL_BIAS_N) b = p.bias[n];
+      else if (p.bias_mode == NTL_BIAS_MN) b = p.bias[static_cast<int64_t>(m) * p.N + n];
+      else if (p.bias_mode == NTL_BIAS_M) b = p.bias[m];
+      p.c[static_cast<int64_t>(m) * p.N + n] = epi(acc[i][j], p.alpha, b, p.relu, p.bias_mode);
+    }
+  }
+}
+
+// ------------------------------------------------------------------ host side
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(ptr);
+  });
+  return fn;
+}
+
+// 2-D fp16 tensor map over a row-major [rows, cols] matrix, box {box_cols, box_rows}.
+int make_map_f16(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols, uint32_t box_cols,
+                 uint32_t box_rows) {
+  EncodeTiledFn fn = encode_fn();
+  if (fn == nullptr) return ntl_fail(NTL_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
+  cuuint64_t dims[2] = {cols, rows};
+  cuuint64_t strides[1] = {cols * 2};
+  cuuint32_t box[2] = {box_cols, box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return ntl_fail(NTL_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", int(r));
+  return NTL_OK;
+}
+
+// The dynamic shared-memory opt-in is a per-device function attribute: set it once per
+// device (the first call on a device must not be inside a stream capture).
+int ensure_smem_attr() {
+  static std::atomic<uint64_t> done_mask{0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return ntl_fail(NTL_ERR_CUDA, "cudaGetDevice failed");
+  const uint64_t bit = dev < 64 ? (uint64_t(1) << dev) : 0;
+  if (bit && (done_mask.load(std::memory_order_acquire) & bit)) return NTL_OK;
+  cudaError_t e = cudaFuncSetAttribute(gemm_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+  if (e != cudaSuccess) return ntl_fail(NTL_ERR_CUDA, "cudaFuncSetAttribute(gemm): %s", cudaGetErrorString(e));
+  done_mask.fetch_or(bit, std::memory_order_release);
+  return NTL_OK;
+}
+
+}  // namespace
+
+uint32_t ntl_gemm_status_read(int clear) {
+  uint32_t v = 0;
+  if (cudaMemcpyFromSymbol(&v, g_gemm_status, sizeof(v)) != cudaSuccess) return 0;
+  if (clear) {
+    uint32_t z = 0;
+    cudaMemcpyToSymbol(g_gemm_status, &z, sizeof(z));
+  }
+  return v;
+}
+
+extern "C" int ntl_gemm_f16_f32(const uint16_t* a, const uint16_t* b, float* c, const float* bias, int bias_mode,
+                                float alpha, int relu, int64_t M, int64_t N, int64_t K, int b_trans,
+                                ntl_stream_t stream) {
+  NTL_REQUIRE(M >= 0 && N >= 0 && K >= 0, NTL_ERR_INVALID, "gemm: negative size");
+  NTL_REQUIRE(M < (int64_t(1) << 31) && N < (int64_t(1) << 31) && K < (int64_t(1) << 31), NTL_ERR_UNSUPPORTED,
+              "gemm: dimensions must be < 2^31");
+  NTL_REQUIRE(bias_mode >= NTL_BIAS_NONE && bias_mode <= NTL_BIAS_M, NTL_ERR_INVALID, "gemm: bad bias_mode %d",
+              bias_mode);
+  NTL_REQUIRE(bias_mode == NTL_BIAS_NONE || bias != nullptr, NTL_ERR_INVALID, "gemm: bias_mode needs a bias pointer");
+  if (M == 0 || N == 0) return NTL_OK;
+  NTL_REQUIRE(c && (K == 0 || (a && b)), NTL_ERR_INVALID, "gemm: NULL pointer");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  GemmParams p;
+  p.c = c;
+  p.bias = bias;
+  p.bias_mode = bias_mode;
+  p.alpha = alpha;
+  p.relu = relu ? 1 : 0;
+  p.M = static_cast<int>(M), p.N = static_cast<int>(N), p.K = static_cast<int>(K);
+  p.b_trans = b_trans ? 1 : 0;
+  p.vec_store = (N % 4 == 0 && ntl_aligned(c, 16)) ? 1 : 0;
+  p.wait_limit = ntl_wait_limit();
+  const bool tma_ok = K > 0 && K % 8 == 0 && (b_trans || N % 8 == 0) && ntl_aligned(a, 16) && ntl_aligned(b, 16);
+  if (!tma_ok) {
+    dim3 grid(static_cast<unsigned>((N + FB_T - 1) / FB_T), static_cast<unsigned>((M + FB_T - 1) / FB_T));
+    NTL_REQUIRE(grid.y <= 65535, NTL_ERR_UNSUPPORTED, "gemm: M too large for the unaligned path");
+    gemm_simt_kernel<<<grid, 256, 0, s>>>(reinterpret_cast<const __half*>(a), reinterpret_cast<const __half*>(b), p);
+    ntl_note_launch();
+    return ntl_check_launch("gemm (CUDA-core path) launch");
+  }
+  CUtensorMap ma, mb;
+  if (int rc = make_map_f16(&ma, a, M, K, BK, BM)) return rc;
+  if (b_trans) {
+    if (int rc = make_map_f16(&mb, b, N, K, BK, BN)) return rc;
+  } else {
+    if (int rc = make_map_f16(&mb, b, K, N, 64, BK)) return rc;
+  }
+  if (int rc = ensure_smem_attr()) return rc;
+  int sms = 0;
+  if (int rc = ntl_num_sms(&sms)) return rc;
+  const int64_t tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
+  NTL_REQUIRE(tiles < (int64_t(1) << 31), NTL_ERR_UNSUPPORTED, "gemm: too many tiles");
+  const int grid = static_cast<int>(tiles < sms ? tiles : sms);
+  gemm_tc_kernel<<<grid, THREADS, SMEM_BYTES, s>>>(ma, mb, p);
+  ntl_note_launch();
+  return ntl_check_launch("gemm (tcgen05 path) launch");
+}

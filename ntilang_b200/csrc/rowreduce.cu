@@ -1,0 +1,316 @@
+// Row reductions: softmax and RMSNorm over [rows, cols] fp32.
+//
+// Reference (python/ntilang/codegen.py:1028-1240, examples/softmax.py:9-25,
+// examples/rmsnorm.py:13-37): the tile row is padded to P = next_pow2(cols) with the op's
+// padding value (-inf for softmax, 0 for RMSNorm), and row sums are a perfect binary tree
+// over those P positions in column order: the warp shuffle-down tree over 32 consecutive
+// columns followed by the pairwise tree over the 32-column groups (codegen.py:1094-1151).
+//
+// Layout here: lane l of a row's warp holds columns [128c + 4l, 128c + 4l + 4) for chunk
+// c.  Position bits, low to high, are (element: 2 bits, lane: 5 bits, chunk), so the same
+// perfect tree is: in-lane pairs (e0+e1)+(e2+e3), then xor-shuffle levels 1..16 (both lanes
+// of a pair form the identical commutative sum), then pairwise over chunks.  Padding
+// beyond cols contributes exact zeros (exp(-inf) = 0, 0^2 = 0), and t + 0 == t for the
+// non-negative sums involved, so rounding to the next power of two of chunks is free.
+// Maxima are order-independent (fmaxf).  One row is one warp; rows longer than 2048
+// columns use one 256-thread CTA per row with the warp level of the tree in shared memory.
+#include <math_constants.h>
+
+#include "ntl_common.cuh"
+
+namespace {
+
+constexpr unsigned kFull = 0xffffffffu;
+constexpr int kWarpsPerBlock = 8;
+
+template <bool VEC>
+__device__ __forceinline__ void load4(const float* __restrict__ row, int64_t col, int64_t cols, float pad,
+                                      float (&v)[4]) {
+  if (VEC && col + 3 < cols) {
+    float4 t = __ldcs(reinterpret_cast<const float4*>(row + col));
+    v[0] = t.x, v[1] = t.y, v[2] = t.z, v[3] = t.w;
+  } else {
+#pragma unroll
+    for (int e = 0; e < 4; ++e) v[e] = (col + e < cols) ? __ldcs(row + col + e) : pad;
+  }
+}
+
+template <bool VEC>
+__device__ __forceinline__ void store4(float* __restrict__ row, int64_t col, int64_t cols, const float (&v)[4]) {
+  if (VEC && col + 3 < cols) {
+    __stcs(reinterpret_cast<float4*>(row + col), make_float4(v[0], v[1], v[2], v[3]));
+  } else {
+#pragma unroll
+    for (int e = 0; e < 4; ++e)
+      if (col + e < cols) __stcs(row + col + e, v[e]);
+  }
+}
+
+__device__ __forceinline__ float lane_pair_sum(const float (&v)[4]) {
+  return __fadd_rn(__fadd_rn(v[0], v[1]), __fadd_rn(v[2], v[3]));
+}
+
+__device__ __forceinline__ float warp_tree_sum(float s) {
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) s = __fadd_rn(s, __shfl_xor_sync(kFull, s, o));
+  return s;
+}
+
+__device__ __forceinline__ float warp_max(float m) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(kFull, m, o));
+  return m;
+}
+
+// Perfect tree over N partial sums (N a power of two after implicit zero padding).
+template <int N>
+__device__ __forceinline__ float chunk_tree(float (&s)[N]) {
+#pragma unroll
+  for (int w = 1; w < N; w <<= 1) {
+#pragma unroll
+    for (int c = 0; c + w < N; c += 2 * w) s[c] = __fadd_rn(s[c], s[c + w]);
+  }
+  return s[0];
+}
+
+// ------------------------------------------------------------------------- softmax
+
+template <int NCH, bool VEC>
+__global__ void __launch_bounds__(kWarpsPerBlock * 32) softmax_rows_warp(const float* __restrict__ x,
+                                                                         float* __restrict__ y, int64_t rows,
+                                                                         int64_t cols) {
+  const int lane = threadIdx.x & 31;
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * kWarpsPerBlock + (threadIdx.x >> 5);
+  if (row >= rows) return;
+  const float* xr = x + row * cols;
+  float* yr = y + row * cols;
+  float v[NCH][4];
+#pragma unroll
+  for (int c = 0; c < NCH; ++c) load4<VEC>(xr, static_cast<int64_t>(c) * 128 + lane * 4, cols, -CUDART_INF_F, v[c]);
+  float m = -CUDART_INF_F;
+#pragma unroll
+  for (int c = 0; c < NCH; ++c)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) m = fmaxf(m, v[c][e]);
+  m = warp_max(m);
+  float s[NCH];
+#pragma unroll
+  for (int c = 0; c < NCH; ++c) {
+#pragma unroll
+    for (int e = 0; e < 4; ++e) v[c][e] = expf(__fsub_rn(v[c][e], m));
+    s[c] = warp_tree_sum(lane_pair_sum(v[c]));
+  }
+  const float total = chunk_tree<NCH>(s);
+#pragma unroll
+  for (int c = 0; c < NCH; ++c) {
+#pragma unroll
+    for (int e = 0; e < 4; ++e) v[c][e] = __fdiv_rn(v[c][e], total);
+    store4<VEC>(yr, static_cast<int64_t>(c) * 128 + lane * 4, cols, v[c]);
+  }
+}
+
+// One CTA (8 warps) per row; position bits (element 2, lane 5, warp 3, chunk).
+template <int NCH, bool VEC>
+__global__ void __launch_bounds__(256) softmax_rows_cta(const float* __restrict__ x, float* __restrict__ y,
+                                                        int64_t rows, int64_t cols) {
+  __shared__ float red[NCH][8];
+  __shared__ float red_max[8];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int64_t row = blockIdx.x;
+  const float* xr = x + row * cols;
+  float* yr = y + row * cols;
+  float v[NCH][4];
+#pragma unroll
+  for (int c = 0; c < NCH; ++c)
+    load4<VEC>(xr, static_cast<int64_t>(c) * 1024 + threadIdx.x * 4, cols, -CUDART_INF_F, v[c]);
+  float m = -CUDART_INF_F;
+#pragma unroll
+  for (int c = 0; c < NCH; ++c)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) m = fmaxf(m, v[c][e]);
+  m = warp_max(m);
+  if (lane == 0) red_max[warp] = m;
+  __syncthreads();
+  m = red_max[0];
+#pragma unroll
+  for (int w = 1; w < 8; ++w) m = fmaxf(m, red_max[w]);
+#pragma unroll
+  for (int c = 0; c < NCH; ++c) {
+#pragma unroll
+    for (int e = 0; e < 4; ++e) v[c][e] = expf(__fsub_rn(v[c][e], m));
+    float s = warp_tree_sum(lane_pair_sum(v[c]));
+    if (lane == 0) red[c][warp] = s;
+  }
+  __syncthreads();
+  float s[NCH];
+#pragma unroll
+  for (int c = 0; c < NCH; ++c) {
+    float t[8];
+#pragma unroll
+    for (int w = 0; w < 8; ++w) t[w] = red[c][w];
+    s[c] = chunk_tree<8>(t);
+  }
+  const float total = chunk_tree<NCH>(s);
+#pragma unroll
+  for (int c = 0; c < NCH; ++c) {
+#pragma unroll
+    for (int e = 0; e < 4; ++e) v[c][e] = __fdiv_rn(v[c][e], total);
+    store4<VEC>(yr, static_cast<int64_t>(c) * 1024 + threadIdx.x * 4, cols, v[c]);
+  }
+}
+
+// ------------------------------------------------------------------------- RMSNorm
+
+template <int NCH, bool VEC>
+__global__ void __launch_bounds__(kWarpsPerBlock * 32) rmsnorm_rows_warp(const float* __restrict__ x,
+                                                                         const float* __restrict__ w,
+                                                                         float* __restrict__ y, int64_t rows,
+                                                                         int64_t cols, float eps, float inv_n) {
+  const int lane = threadIdx.x & 31;
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * kWarpsPerBlock + (threadIdx.x >> 5);
+  if (row >= rows) return;
+  const float* xr = x + row * cols;
+  float* yr = y + row * cols;
+  float v[NCH][4];
+#pragma unroll
+  for (int c = 0; c < NCH; ++c) load4<VEC>(xr, static_cast<int64_t>(c) * 128 + lane * 4, cols, 0.0f, v[c]);
+  float s[NCH];
+#pragma unroll
+  for (int c = 0; c < NCH; ++c) {
+    float q[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) q[e] = __fmul_rn(v[c][e], v[c][e]);
+    s[c] = warp_tree_sum(lane_pair_sum(q));
+  }
+  const float ss = chunk_tree<NCH>(s);
+  const float inv = rsqrtf(__fadd_rn(__fmul_rn(ss, inv_n), eps));
+#pragma unroll
+  for (int c = 0; c < NCH; ++c) {
+    const int64_t col = static_cast<int64_t>(c) * 128 + lane * 4;
+    float wv[4];
+    if (VEC && col + 3 < cols) {
+      float4 t = __ldg(reinterpret_cast<const float4*>(w + col));
+      wv[0] = t.x, wv[1] = t.y, wv[2] = t.z, wv[3] = t.w;
+    } else {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) wv[e] = (col + e < cols) ? __ldg(w + col + e) : 0.0f;
+    }
+#pragma unroll
+    for (int e = 0; e < 4; ++e) v[c][e] = __fmul_rn(__fmul_rn(v[c][e], inv), wv[e]);
+    store4<VEC>(yr, col, cols, v[c]);
+  }
+}
+
+template <int NCH, bool VEC>
+__global__ void __launch_bounds__(256) rmsnorm_rows_cta(const float* __restrict__ x, const float* __restrict__ w,
+                                                        float* __restrict__ y, int64_t rows, int64_t cols, float eps,
+                                                        float inv_n) {
+  __shared__ float red[NCH][8];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int64_t row = blockIdx.x;
+  const float* xr = x + row * cols;
+  float* yr = y + row * cols;
+  float v[NCH][4];
+#pragma unroll
+  for (int c = 0; c < NCH; ++c) load4<VEC>(xr, static_cast<int64_t>(c) * 1024 + threadIdx.x * 4, cols, 0.0f, v[c]);
+#pragma unroll
+  for (int c = 0; c < NCH; ++c) {
+    float q[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) q[e] = __fmul_rn(v[c][e], v[c][e]);
+    float s = warp_tree_sum(lane_pair_sum(q));
+    if (lane == 0) red[c][warp] = s;
+  }
+  __syncthreads();
+  float s[NCH];
+#pragma unroll
+  for (int c = 0; c < NCH; ++c) {
+    float t[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) t[k] = red[c][k];
+    s[c] = chunk_tree<8>(t);
+  }
+  const float ss = chunk_tree<NCH>(s);
+  const float inv = rsqrtf(__fadd_rn(__fmul_rn(ss, inv_n), eps));
+#pragma unroll
+  for (int c = 0; c < NCH; ++c) {
+    const int64_t col = static_cast<int64_t>(c) * 1024 + threadIdx.x * 4;
+    float wv[4];
+    if (VEC && col + 3 < cols) {
+      float4 t = __ldg(reinterpret_cast<const float4*>(w + col));
+      wv[0] = t.x, wv[1] = t.y, wv[2] = t.z, wv[3] = t.w;
+    } else {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) wv[e] = (col + e < cols) ? __ldg(w + col + e) : 0.0f;
+    }
+#pragma unroll
+    for (int e = 0; e < 4; ++e) v[c][e] = __fmul_rn(__fmul_rn(v[c][e], inv), wv[e]);
+    store4<VEC>(yr, col, cols, v[c]);
+  }
+}
+
+// --------------------------------------------------------------------- dispatch
+
+constexpr int64_t kMaxWarpCols = 2048;   // 16 chunks of 128 per warp
+constexpr int64_t kMaxCtaCols = 16384;   // 16 chunks of 1024 per CTA
+
+template <class WarpK, class CtaK>
+struct Dispatch;
+
+#define NTL_ROW_DISPATCH(KW, KC, VEC, ...)                                                              \
+  do {                                                                                                  \
+    const int64_t nch = (cols + 127) / 128;                                                             \
+    if (cols <= kMaxWarpCols) {                                                                         \
+      const int64_t blocks = (rows + kWarpsPerBlock - 1) / kWarpsPerBlock;                              \
+      NTL_REQUIRE(blocks <= 0x7fffffff, NTL_ERR_UNSUPPORTED, "too many rows");                         \
+      dim3 g(static_cast<unsigned>(blocks)), b(kWarpsPerBlock * 32);                                    \
+      if (nch <= 1) KW<1, VEC><<<g, b, 0, s>>>(__VA_ARGS__);                                            \
+      else if (nch <= 2) KW<2, VEC><<<g, b, 0, s>>>(__VA_ARGS__);                                       \
+      else if (nch <= 4) KW<4, VEC><<<g, b, 0, s>>>(__VA_ARGS__);                                       \
+      else if (nch <= 8) KW<8, VEC><<<g, b, 0, s>>>(__VA_ARGS__);                                       \
+      else KW<16, VEC><<<g, b, 0, s>>>(__VA_ARGS__);                                                    \
+    } else {                                                                                            \
+      NTL_REQUIRE(rows <= 0x7fffffff, NTL_ERR_UNSUPPORTED, "too many rows");                           \
+      const int64_t cch = (cols + 1023) / 1024;                                                         \
+      dim3 g(static_cast<unsigned>(rows)), b(256);                                                      \
+      if (cch <= 2) KC<2, VEC><<<g, b, 0, s>>>(__VA_ARGS__);                                            \
+      else if (cch <= 4) KC<4, VEC><<<g, b, 0, s>>>(__VA_ARGS__);                                       \
+      else if (cch <= 8) KC<8, VEC><<<g, b, 0, s>>>(__VA_ARGS__);                                       \
+      else KC<16, VEC><<<g, b, 0, s>>>(__VA_ARGS__);                                                    \
+    }                                                                                                   \
+  } while (0)
+
+}  // namespace
+
+extern "C" int ntl_softmax_f32(const float* x, float* y, int64_t rows, int64_t cols, ntl_stream_t stream) {
+  NTL_REQUIRE(rows >= 0 && cols >= 0, NTL_ERR_INVALID, "softmax: negative size");
+  if (rows == 0 || cols == 0) return NTL_OK;
+  NTL_REQUIRE(x && y, NTL_ERR_INVALID, "softmax: NULL pointer");
+  NTL_REQUIRE(cols <= kMaxCtaCols, NTL_ERR_UNSUPPORTED, "softmax: rows longer than %lld columns are not supported",
+              (long long)kMaxCtaCols);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const bool vec = (cols % 4 == 0) && ntl_aligned(x, 16) && ntl_aligned(y, 16);
+  if (vec)
+    NTL_ROW_DISPATCH(softmax_rows_warp, softmax_rows_cta, true, x, y, rows, cols);
+  else
+    NTL_ROW_DISPATCH(softmax_rows_warp, softmax_rows_cta, false, x, y, rows, cols);
+  ntl_note_launch();
+  return ntl_check_launch("softmax launch");
+}
+
+extern "C" int ntl_rmsnorm_f32(const float* x, const float* w, float* y, int64_t rows, int64_t cols, float eps,
+                               float inv_n, ntl_stream_t stream) {
+  NTL_REQUIRE(rows >= 0 && cols >= 0, NTL_ERR_INVALID, "rmsnorm: negative size");
+  if (rows == 0 || cols == 0) return NTL_OK;
+  NTL_REQUIRE(x && w && y, NTL_ERR_INVALID, "rmsnorm: NULL pointer");
+  NTL_REQUIRE(cols <= kMaxCtaCols, NTL_ERR_UNSUPPORTED, "rmsnorm: rows longer than %lld columns are not supported",
+              (long long)kMaxCtaCols);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const bool vec = (cols % 4 == 0) && ntl_aligned(x, 16) && ntl_aligned(y, 16) && ntl_aligned(w, 16);
+  if (vec)
+    NTL_ROW_DISPATCH(rmsnorm_rows_warp, rmsnorm_rows_cta, true, x, w, y, rows, cols, eps, inv_n);
+  else
+    NTL_ROW_DISPATCH(rmsnorm_rows_warp, rmsnorm_rows_cta, false, x, w, y, rows, cols, eps, inv_n);
+  ntl_note_launch();
+  return ntl_check_launch("rmsnorm launch");
+}

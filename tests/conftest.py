@@ -1,0 +1,54 @@
+"""Shared pytest configuration.
+
+Markers: ``gpu`` — needs a CUDA device (run with ``-m gpu`` on a B200); everything else
+runs on CPU.  The GPU tests call the sm_100a kernels through the C ABI of
+libntl_kernels.so (via the ntilang-compatible Python surface) and compare with the CPU
+oracle under ``oracle/`` and the golden vectors under ``tests/golden/``.
+"""
+
+from __future__ import annotations
+
+import os
+import sys
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+ROOT = Path(__file__).resolve().parents[1]
+GOLDEN = ROOT / "tests" / "golden"
+if str(ROOT) not in sys.path:
+    sys.path.insert(0, str(ROOT))
+
+
+def pytest_configure(config):
+    config.addinivalue_line("markers", "gpu: requires an NVIDIA GPU (sm_100a)")
+    config.addinivalue_line("markers", "slow: long-running CPU test")
+
+
+def golden(name: str) -> dict:
+    with np.load(GOLDEN / f"{name}.npz") as data:
+        return {k: data[k] for k in data.files}
+
+
+@pytest.fixture(scope="session")
+def torch_cuda():
+    torch = pytest.importorskip("torch")
+    if not torch.cuda.is_available():
+        pytest.skip("No NVIDIA GPU available")
+    from ntilang_b200 import _lib
+
+    _lib.lib()  # the CUDA path must be the one that runs: fail loudly if the library is missing
+    return torch
+
+
+@pytest.fixture(scope="session")
+def built_library():
+    """Build (if needed) and return the path of libntl_kernels.so (CPU-safe: no device calls)."""
+    from ntilang_b200.build import LIB, build_library
+
+    if os.environ.get("NTL_SKIP_BUILD") != "1":
+        build_library()
+    if not LIB.exists():
+        pytest.skip("libntl_kernels.so is not built")
+    return LIB

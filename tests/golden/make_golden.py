@@ -1,0 +1,142 @@
+"""Generate golden vectors from the reference implementation itself.
+
+Run once, in a container where the reference checkout is present:
+
+    python tests/golden/make_golden.py --reference <path-to-Ntilang-checkout>
+
+It imports the reference package (``python/ntilang``) and its ``examples/*.py`` kernels,
+evaluates each kernel with the reference's own serial NumPy evaluator
+``ntilang.testing.reference`` (python/ntilang/testing.py:34) — and, for a larger
+bit-exact scan case, ``ntilang.scan.evaluate`` (scan.py:349-389) — on seeded inputs, and
+writes ``tests/golden/<case>.npz`` with the inputs, outputs and parameters.  The tests
+and the GPU box only read the committed ``.npz`` files; nothing imports the reference at
+test time.
+"""
+
+from __future__ import annotations
+
+import argparse
+import importlib.util
+import sys
+import time
+from pathlib import Path
+
+import numpy as np
+
+HERE = Path(__file__).resolve().parent
+
+
+def load_example(ref: Path, name: str):
+    spec = importlib.util.spec_from_file_location(f"ref_example_{name}", ref / "examples" / f"{name}.py")
+    module = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(module)
+    return module
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--reference", required=True, type=Path)
+    args = ap.parse_args()
+    ref = args.reference.resolve()
+    # The reference package is also called `ntilang`: make sure it, not this repo's alias, is imported.
+    sys.path = [str(ref / "python")] + [p for p in sys.path if Path(p or ".").resolve() != HERE.parents[1]]
+    import ntilang  # noqa: F401  (the reference)
+    from ntilang import scan as ref_scan
+    from ntilang.testing import reference
+
+    assert Path(ntilang.__file__).resolve().is_relative_to(ref), ntilang.__file__
+
+    def save(name, **arrays):
+        np.savez_compressed(HERE / f"{name}.npz", **arrays)
+        print("wrote", name, {k: getattr(v, "shape", v) for k, v in arrays.items()})
+
+    t0 = time.time()
+    # vector add (examples/vector_add.py)
+    va = load_example(ref, "vector_add")
+    rng = np.random.default_rng(0)
+    a = rng.normal(size=1000).astype(np.float32)
+    b = rng.normal(size=1000).astype(np.float32)
+    c = np.full_like(a, np.nan)
+    reference(va.vector_add(n=1000, block=128), a, b, c)
+    save("vadd_1000", a=a, b=b, c=c)
+
+    # cumsum (examples/cumsum.py), forward and reverse
+    cs = load_example(ref, "cumsum")
+    for rows, cols, seed in ((7, 65, 1), (4, 256, 2)):
+        rng = np.random.default_rng(seed)
+        x = rng.uniform(-1, 1, size=(rows, cols)).astype(np.float32)
+        for rev in (False, True):
+            y = np.full_like(x, np.nan)
+            reference(cs.cumsum(rows, cols, reverse=rev), x, y)
+            save(f"cumsum_{rows}x{cols}_{'rev' if rev else 'fwd'}", x=x, y=y, reverse=np.array(rev))
+    # special values (signed zeros, infinities, NaN) like the reference's scan tests
+    rng = np.random.default_rng(407)
+    x = (rng.normal(size=(3, 97)) * 30).astype(np.float32)
+    x[0, :6] = [0.0, -0.0, np.inf, -np.inf, np.nan, np.nan]
+    x[1, :] = np.nan
+    x[2, :5] = [-0.0, -0.0, -0.0, 1e38, 1e38]
+    for rev in (False, True):
+        y = np.full_like(x, 7.0)
+        with np.errstate(over="ignore", invalid="ignore"):
+            reference(cs.cumsum(3, 97, reverse=rev), x, y)
+        save(f"cumsum_special_{'rev' if rev else 'fwd'}", x=x, y=y, reverse=np.array(rev))
+    # a larger scan case through the reference's scan evaluator (the device order)
+    rng = np.random.default_rng(3)
+    x = rng.uniform(-1, 1, size=(64, 1000)).astype(np.float32)
+    for rev in (False, True):
+        y = ref_scan.evaluate(x, "sum", 1, rev)
+        save(f"cumsum_eval_64x1000_{'rev' if rev else 'fwd'}", x=x, y=y, reverse=np.array(rev))
+
+    # softmax (examples/softmax.py)
+    sm = load_example(ref, "softmax")
+    for rows, cols, seed, scale in ((9, 113, 491, 100.0), (4, 512, 4, 2.0)):
+        rng = np.random.default_rng(seed)
+        x = (rng.normal(size=(rows, cols)) * scale).astype(np.float32)
+        y = np.full_like(x, np.nan)
+        reference(sm.softmax(rows, cols), x, y)
+        save(f"softmax_{rows}x{cols}", x=x, y=y)
+
+    # RMSNorm (examples/rmsnorm.py)
+    rn = load_example(ref, "rmsnorm")
+    for rows, cols, seed in ((6, 1024, 5), (5, 768, 6)):
+        rng = np.random.default_rng(seed)
+        x = rng.normal(size=(rows, cols)).astype(np.float32)
+        w = rng.normal(1.0, 0.1, size=cols).astype(np.float32)
+        y = np.full_like(x, np.nan)
+        reference(rn.rmsnorm(rows, cols, eps=1e-6), x, w, y)
+        save(f"rmsnorm_{rows}x{cols}", x=x, w=w, y=y, eps=np.array(1e-6))
+
+    # GEMM (examples/matmul.py) and GEMM + bias + ReLU (examples/matmul_relu.py)
+    mm = load_example(ref, "matmul")
+    rng = np.random.default_rng(11)
+    a = rng.normal(size=(65, 37)).astype(np.float16)
+    b = rng.normal(size=(37, 71)).astype(np.float16)
+    c = np.full((65, 71), np.nan, np.float32)
+    reference(mm.matmul(), a, b, c)
+    save("gemm_65x71x37", a=a, b=b, c=c)
+    mr = load_example(ref, "matmul_relu")
+    rng = np.random.default_rng(61)
+    a = rng.normal(size=(65, 37)).astype(np.float16)
+    b = rng.normal(size=(37, 71)).astype(np.float16)
+    bias = rng.normal(size=(65, 71)).astype(np.float32)
+    c = np.full((65, 71), np.nan, np.float32)
+    reference(mr.matmul_relu(), a, b, bias, c)
+    save("gemm_relu_65x71x37", a=a, b=b, bias=bias, c=c, alpha=np.array(0.5))
+
+    # FlashAttention-2 forward (examples/flash_attention.py), non-causal and causal
+    fa = load_example(ref, "flash_attention")
+    for causal in (False, True):
+        rng = np.random.default_rng(21 + int(causal))
+        shape = (1, 2, 128, 64)
+        q, k, v = ((rng.normal(size=shape) * 0.5).astype(np.float16) for _ in range(3))
+        o = np.full(shape, np.nan, np.float16)
+        kern = fa.flash_attention(1, 2, 128, 64, is_causal=causal)
+        reference(kern, q, k, v, o)
+        scale = (1.0 / np.sqrt(64)) * 1.44269504
+        save(f"fa2_1x2x128x64_{'causal' if causal else 'full'}", q=q, k=k, v=v, o=o, scale_log2=np.array(scale),
+             causal=np.array(causal))
+    print(f"done in {time.time() - t0:.1f} s")
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,224 @@
+"""GPU parity for the memory-bound families: vector add, cumsum, softmax, RMSNorm.
+
+Every kernel runs through the reference-compatible surface (``ntilang.compile`` / ``jit``
+factories -> ``CompiledKernel.__call__`` -> the C ABI of libntl_kernels.so) and is compared
+with the CPU oracle (``oracle/``) and the golden vectors generated from the reference.
+
+Bars (north star): vector add and cumsum bit-exact; softmax and RMSNorm within 1e-5
+relative (an absolute floor of 1e-30 covers results that underflow to subnormals).
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+from ntilang_b200 import kernels as K
+from oracle import ntl_oracle as O
+from oracle import rowops
+from tests.conftest import golden
+
+pytestmark = pytest.mark.gpu
+
+
+def bits_equal(actual, expected):
+    a = np.ascontiguousarray(actual, np.float32)
+    e = np.ascontiguousarray(expected, np.float32)
+    same = (a.view(np.uint32) == e.view(np.uint32)) | (np.isnan(a) & np.isnan(e))
+    return bool(same.all()), int((~same).sum())
+
+
+def to_gpu(torch, arr):
+    return torch.from_numpy(np.ascontiguousarray(arr)).cuda()
+
+
+# --------------------------------------------------------------------------- vector add
+
+
+def test_vector_add_golden(torch_cuda):
+    torch = torch_cuda
+    g = golden("vadd_1000")
+    out = K.vector_add(1000)(to_gpu(torch, g["a"]), to_gpu(torch, g["b"]))
+    ok, bad = bits_equal(out.cpu().numpy(), g["c"])
+    assert ok, bad
+
+
+@pytest.mark.parametrize("n", [1, 3, 4, 1000, 4099, 16 * 1024 * 1024 + 3])
+def test_vector_add_bit_exact(torch_cuda, n):
+    torch = torch_cuda
+    g = torch.Generator(device="cuda").manual_seed(n)
+    a = torch.randn(n, device="cuda", generator=g)
+    b = torch.randn(n, device="cuda", generator=g)
+    c = K.vector_add(n)(a, b)
+    torch.testing.assert_close(c, a + b, rtol=0, atol=0)
+
+
+def test_vector_add_unaligned_pointers_abi(torch_cuda):
+    """The C ABI also serves unaligned pointers (scalar path); results stay bit-exact."""
+    torch = torch_cuda
+    from ntilang_b200 import _lib
+
+    base = torch.randn(3 * 1001 + 8, device="cuda")
+    a, b, c = base[1:1001], base[1002:2002], torch.empty(1003, device="cuda")[3:1003]
+    _lib.call("ntl_vadd_f32", a.data_ptr(), b.data_ptr(), c.data_ptr(), 1000, torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    torch.testing.assert_close(c, a + b, rtol=0, atol=0)
+
+
+def test_nondefault_stream(torch_cuda):
+    torch = torch_cuda
+    kernel = K.vector_add(1000)
+    stream = torch.cuda.Stream()
+    with torch.cuda.stream(stream):
+        a = torch.full((1000,), 2.0, device="cuda")
+        b = torch.full_like(a, 3.0)
+        c = kernel(a, b)
+        expected = a + b
+    stream.synchronize()
+    torch.testing.assert_close(c, expected, rtol=0, atol=0)
+
+
+# ------------------------------------------------------------------------------- cumsum
+
+
+@pytest.mark.parametrize("case", [
+    "cumsum_7x65_fwd", "cumsum_7x65_rev", "cumsum_4x256_fwd", "cumsum_4x256_rev",
+    "cumsum_special_fwd", "cumsum_special_rev", "cumsum_eval_64x1000_fwd", "cumsum_eval_64x1000_rev",
+])
+def test_cumsum_golden_bit_exact(torch_cuda, case):
+    torch = torch_cuda
+    g = golden(case)
+    rows, cols = g["x"].shape
+    y = K.cumsum(rows, cols, bool(g["reverse"]))(to_gpu(torch, g["x"]))
+    ok, bad = bits_equal(y.cpu().numpy(), g["y"])
+    assert ok, f"{bad} elements differ"
+
+
+@pytest.mark.parametrize("rows,cols", [(1, 1), (3, 2), (5, 3), (2, 31), (9, 33), (4, 127), (3, 129),
+                                       (6, 1000), (2, 1025), (3, 4097), (2, 70001)])
+@pytest.mark.parametrize("reverse", [False, True])
+def test_cumsum_ragged_bit_exact(torch_cuda, rows, cols, reverse):
+    torch = torch_cuda
+    rng = np.random.default_rng(rows * 7919 + cols)
+    x = rng.uniform(-1, 1, size=(rows, cols)).astype(np.float32)
+    y = K.cumsum(rows, cols, reverse)(to_gpu(torch, x)).cpu().numpy()
+    ok, bad = bits_equal(y, O.cumsum_rows(x, reverse))
+    assert ok, f"{bad} elements differ"
+
+
+@pytest.mark.parametrize("reverse", [False, True])
+def test_cumsum_baseline_size_bit_exact(torch_cuda, reverse):
+    """BASELINE config: X f32 [32768, 256] ~ U(-1, 1)."""
+    torch = torch_cuda
+    g = torch.Generator(device="cuda").manual_seed(0)
+    x = torch.rand(32768, 256, device="cuda", generator=g) * 2 - 1
+    y = K.cumsum(32768, 256, reverse)(x)
+    ok, bad = bits_equal(y.cpu().numpy(), rowops.cumsum(x.cpu().numpy(), reverse))
+    assert ok, f"{bad} elements differ"
+
+
+def test_cumsum_1d_program(torch_cuda):
+    """A rank-1 tile scan (one row) written directly with ntilang.compile."""
+    torch = torch_cuda
+    import ntilang
+    import ntilang.language as T
+
+    @T.prim_func
+    def scan1d(A: T.Tensor((300,), "float32"), B: T.Tensor((300,), "float32")):
+        with T.Kernel(1, threads=128):
+            t = T.alloc_shared((300,), "float32")
+            T.copy(A, t)
+            T.cumsum(t, dim=0)
+            T.copy(t, B)
+
+    k = ntilang.compile(scan1d)
+    x = np.random.default_rng(1).normal(size=300).astype(np.float32)
+    out = torch.empty(300, device="cuda")
+    k(to_gpu(torch, x), out)
+    ok, bad = bits_equal(out.cpu().numpy(), O.cumsum_rows(x))
+    assert ok, bad
+
+
+# ------------------------------------------------------------------------------ softmax
+
+
+@pytest.mark.parametrize("case", ["softmax_9x113", "softmax_4x512"])
+def test_softmax_golden(torch_cuda, case):
+    torch = torch_cuda
+    g = golden(case)
+    rows, cols = g["x"].shape
+    y = K.softmax(rows, cols)(to_gpu(torch, g["x"])).cpu().numpy()
+    np.testing.assert_allclose(y, g["y"], rtol=1e-5, atol=1e-30)
+
+
+@pytest.mark.parametrize("rows,cols", [(1, 1), (3, 2), (4, 3), (9, 113), (8, 128), (5, 2047), (7, 2048),
+                                       (3, 2049), (2, 5000), (2, 16384)])
+def test_softmax_shapes(torch_cuda, rows, cols):
+    torch = torch_cuda
+    rng = np.random.default_rng(rows + cols)
+    x = (rng.normal(size=(rows, cols)) * 2.0).astype(np.float32)
+    y = K.softmax(rows, cols)(to_gpu(torch, x)).cpu().numpy()
+    np.testing.assert_allclose(y, O.softmax_rows(x), rtol=1e-5, atol=1e-30)
+
+
+def test_softmax_baseline_size(torch_cuda):
+    """BASELINE config: X f32 [16384, 512] ~ N(0, 4)."""
+    torch = torch_cuda
+    g = torch.Generator(device="cuda").manual_seed(0)
+    x = torch.randn(16384, 512, device="cuda", generator=g) * 2.0
+    y = K.softmax(16384, 512)(x).cpu().numpy()
+    np.testing.assert_allclose(y, rowops.softmax(x.cpu().numpy()), rtol=1e-5, atol=1e-30)
+    np.testing.assert_allclose(y.sum(axis=1), 1.0, rtol=1e-5)
+
+
+def test_softmax_large_magnitude_like_reference(torch_cuda):
+    torch = torch_cuda
+    a = torch.randn(9, 113, device="cuda") * 30
+    y = K.softmax(9, 113)(a)
+    torch.testing.assert_close(y, torch.softmax(a, dim=1), rtol=2e-5, atol=2e-6)
+
+
+# ------------------------------------------------------------------------------ RMSNorm
+
+
+@pytest.mark.parametrize("case", ["rmsnorm_6x1024", "rmsnorm_5x768"])
+def test_rmsnorm_golden(torch_cuda, case):
+    torch = torch_cuda
+    g = golden(case)
+    rows, cols = g["x"].shape
+    y = K.rmsnorm(rows, cols, float(g["eps"]))(to_gpu(torch, g["x"]), to_gpu(torch, g["w"])).cpu().numpy()
+    np.testing.assert_allclose(y, g["y"], rtol=1e-5, atol=1e-7)
+
+
+@pytest.mark.parametrize("rows,cols", [(1, 1), (3, 5), (131, 256), (131, 512), (131, 768), (4, 2048), (3, 3000),
+                                       (2, 16384)])
+def test_rmsnorm_shapes(torch_cuda, rows, cols):
+    torch = torch_cuda
+    rng = np.random.default_rng(rows * cols)
+    x = rng.normal(size=(rows, cols)).astype(np.float32)
+    w = rng.normal(1.0, 0.1, size=cols).astype(np.float32)
+    y = K.rmsnorm(rows, cols, 1e-6)(to_gpu(torch, x), to_gpu(torch, w)).cpu().numpy()
+    np.testing.assert_allclose(y, O.rmsnorm_rows(x, w, 1e-6), rtol=1e-5, atol=1e-7)
+
+
+def test_rmsnorm_baseline_size(torch_cuda):
+    """BASELINE config: X f32 [4096, 1024] ~ N(0,1), gamma ~ N(1, 0.1), eps 1e-6."""
+    torch = torch_cuda
+    g = torch.Generator(device="cuda").manual_seed(0)
+    x = torch.randn(4096, 1024, device="cuda", generator=g)
+    w = torch.randn(1024, device="cuda", generator=g) * 0.1 + 1.0
+    y = K.rmsnorm(4096, 1024, 1e-6)(x, w)
+    np.testing.assert_allclose(y.cpu().numpy(), rowops.rmsnorm(x.cpu().numpy(), w.cpu().numpy(), 1e-6),
+                               rtol=1e-5, atol=1e-7)
+    ref = x * torch.rsqrt(x.pow(2).mean(dim=-1, keepdim=True) + 1e-6) * w
+    torch.testing.assert_close(y, ref, rtol=1e-4, atol=1e-5)
+
+
+def test_native_launches_counted(torch_cuda):
+    torch = torch_cuda
+    from ntilang_b200 import _lib
+
+    before = _lib.launch_count()
+    K.softmax(4, 64)(torch.randn(4, 64, device="cuda"))
+    torch.cuda.synchronize()
+    assert _lib.launch_count() == before + 1
