@@ -429,16 +429,17 @@ def run_op(op, torch, dist, world, steps, warmup, stream, peaks, peak_kind, traf
         for i in range(steps):
             kern(*op.sets[i % nsets][0])
     launches = _lib.launch_count() - before
-    graph.replay()  # untimed replay
-    stream.synchronize()
     start = torch.cuda.Event(enable_timing=True)
     end = torch.cuda.Event(enable_timing=True)
-    if dist is not None:
-        dist.barrier()
-    torch.cuda.synchronize()
-    start.record(stream)
-    graph.replay()
-    end.record(stream)
+    with torch.cuda.stream(stream):  # replay() launches on the current stream
+        graph.replay()  # untimed replay
+        stream.synchronize()
+        if dist is not None:
+            dist.barrier()
+        torch.cuda.synchronize()
+        start.record(stream)
+        graph.replay()
+        end.record(stream)
     torch.cuda.synchronize()
     if dist is not None:
         dist.barrier()
