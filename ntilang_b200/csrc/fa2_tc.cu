@@ -6,18 +6,24 @@
 // (:74-75), O /= l at the end (:77-78); sm_80 mma.sync with smem round trips for the row
 // statistics (codegen.py:972-984, :1062-1073).
 //
-// Design (one CTA = one (batch, head, 128-query tile); 192 threads):
-//   warp 0      TMA: Q once, then K_j / V_j (128 keys x D) into a 2-stage ring.  3-D tensor
-//               maps [B*H, S, D] so rows past S are zero-filled and never cross heads.
-//   warp 1      TMEM owner (512 columns: S double buffer 2x128, O 128) and MMA issuer:
-//               S_j = Q K_j^T (SS, K-major B) is issued before O += P_{j-1} V_{j-1} (SS,
-//               P from smem, V N-major), so QK^T of the next tile overlaps the softmax.
-//   warps 2..5  softmax, one query row per thread (TMEM lane = row): row max of S_j, then
-//               p = exp2(s*c - m*c) into a double-buffered 128B-swizzled fp16 P tile,
-//               l = l*r + sum(p), O *= r in TMEM once P V_{j-1} retired; final O / l -> fp16.
-// Masked scores (causal key > query, keys >= S) contribute exactly 0 like the reference's
-// -1e30 fill.  Every mbarrier wait is bounded; a wait that gives up records a status code,
-// drains in-flight copies and MMAs, frees TMEM and returns.
+// Design: one CTA = one (batch, head, 256-query block) = two 128-row query tiles that
+// share every K/V tile (448 threads, 14 warps):
+//   warps 0-3   softmax of query tile 0, one row per thread (TMEM lane = row)
+//   warps 4-7   softmax of query tile 1
+//   warps 8-11  O correction (rescale in TMEM when a row max moved) and the final
+//               O / l -> fp16 epilogue of both tiles
+//   warp 12     TMEM owner (512 columns: S0, S1, O0, O1) and MMA issuer
+//   warp 13     TMA: Q0, Q1 once, then K_j / V_j (128 keys x D) into a 2-stage ring; 3-D
+//               tensor maps [B*H, S, D] zero-fill rows past S and never cross heads.
+// Per KV tile j the MMA warp issues, per query tile i: O_i += P_i V_j (A = P_i from TMEM,
+// fp16 packed in place over S_i; B = V_j N-major in smem) and then S_i = Q_i K_{j+1}^T
+// (both operands K-major in smem), so the tensor core works on one tile while the other
+// tile's softmax runs.  Softmax uses a lazily updated row max: O and l are rescaled only
+// when the max grows by more than 2^8 (P stays <= 256, exact in the final O / l), and the
+// rescale itself runs in the correction warps.  Masked scores (causal key > query, keys
+// >= S) contribute exactly 0, like the reference's -1e30 fill.  Every mbarrier wait is
+// bounded; a wait that gives up records a status code, drains in-flight copies and
+// MMAs, frees TMEM and returns.
 #include <atomic>
 #include <mutex>
 
@@ -27,45 +33,51 @@ namespace {
 
 __device__ uint32_t g_fa2_status;
 
-constexpr int BM = 128;  // query rows per CTA
-constexpr int BN = 128;  // keys per KV tile
-constexpr int THREADS = 192;
+constexpr int BM = 128;        // rows per query tile
+constexpr int QTILES = 2;      // query tiles per CTA
+constexpr int BQ = BM * QTILES;
+constexpr int BN = 128;        // keys per KV tile
+constexpr int THREADS = 448;
+constexpr int MMA_WARP = 12, TMA_WARP = 13;
 constexpr uint32_t TMEM_COLS = 512;
-constexpr uint32_t S_COL = 0;    // S buffers at columns [0,128) and [128,256)
-constexpr uint32_t O_COL = 256;  // O at [256, 256 + D)
+constexpr float kRescaleLog2 = 8.0f;  // lazy-rescale threshold (log2 units)
 
 struct Fa2Params {
   __half* o;
-  int S, H, n_qt;
+  int S, H, n_qb;
   int causal;
   float c;  // softmax scale in log2 units
   int64_t wait_limit;
 };
 
-struct __align__(8) Fa2Ctl {
+struct __align__(16) Fa2Ctl {
   uint64_t q_full;
   uint64_t k_full[2], v_full[2], kv_empty[2];
-  uint64_t s_full[2], s_free[2];
-  uint64_t p_full;
-  uint64_t o_done;
+  uint64_t s_full[QTILES];
+  uint64_t sm_done[QTILES];
+  uint64_t o_ready[QTILES];
+  uint64_t o_final[QTILES];
   uint64_t drain;
   uint32_t tmem_base;
   int abort;
+  int need[QTILES][4];
+  float scale[QTILES][BM];
+  float lsum[QTILES][BM];
 };
 
 template <int D>
 struct Fa2Smem {
   static constexpr int Q_BYTES = BM * D * 2;
   static constexpr int KV_BYTES = BN * D * 2;
-  static constexpr int P_BYTES = BM * BN * 2;
   static constexpr int Q_OFF = 0;
-  static constexpr int K_OFF = Q_OFF + Q_BYTES;
+  static constexpr int K_OFF = Q_OFF + QTILES * Q_BYTES;
   static constexpr int V_OFF = K_OFF + 2 * KV_BYTES;
-  static constexpr int P_OFF = V_OFF + 2 * KV_BYTES;
-  static constexpr int CTL_OFF = P_OFF + 2 * P_BYTES;
-  static constexpr int USED = CTL_OFF + 256;
+  static constexpr int CTL_OFF = V_OFF + 2 * KV_BYTES;
+  static constexpr int USED = CTL_OFF + static_cast<int>(sizeof(Fa2Ctl));
   // >= 116 KB keeps one CTA per SM, so the 512-column TMEM allocation never contends.
   static constexpr int BYTES = (USED + 1024 > 118784 ? USED + 1024 : 118784);
+  __host__ __device__ static constexpr uint32_t S_COL(int i) { return static_cast<uint32_t>(i * BN); }
+  __host__ __device__ static constexpr uint32_t O_COL(int i) { return static_cast<uint32_t>(2 * BN + i * D); }
 };
 
 __device__ __forceinline__ void fa2_abort(Fa2Ctl* ctl, uint32_t code) {
@@ -73,19 +85,16 @@ __device__ __forceinline__ void fa2_abort(Fa2Ctl* ctl, uint32_t code) {
   *reinterpret_cast<volatile int*>(&ctl->abort) = 1;
 }
 
-// Byte offset of 16-byte chunk `chunk` (0..7) of row `row` inside a 128B-swizzled atom
-// column of 128-byte rows (the layout TMA SWIZZLE_128B writes and UMMA reads).
-__device__ __forceinline__ uint32_t sw128_offset(int row, int chunk) {
-  return static_cast<uint32_t>(row * 128 + ((chunk ^ (row & 7)) << 4));
-}
-
 __device__ __forceinline__ uint32_t pack_half2(float a, float b) {
   __half2 h = __floats2half2_rn(a, b);
   return *reinterpret_cast<uint32_t*>(&h);
 }
 
-__device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
-  asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d) : "memory");
+// Number of KV tiles query tile i of block qb needs (0 when the tile is past S).
+__device__ __forceinline__ int kv_tiles(const Fa2Params& p, int q0_tile) {
+  if (q0_tile >= p.S) return 0;
+  const int all = (p.S + BN - 1) / BN;
+  return p.causal ? min(all, (q0_tile + BM - 1) / BN + 1) : all;
 }
 
 template <int D>
@@ -100,13 +109,14 @@ __global__ void __launch_bounds__(THREADS, 1) fa2_fwd_kernel(const __grid_consta
   volatile int* abort_flag = &ctl->abort;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  // Heavy causal tiles first: the last query tile has the most KV tiles.
-  const int qt = p.causal ? (p.n_qt - 1 - static_cast<int>(blockIdx.x)) : static_cast<int>(blockIdx.x);
-  const int h = blockIdx.y, b = blockIdx.z;
-  const int bh = b * p.H + h;
-  const int q0 = qt * BM;
-  const int n_kv_all = (p.S + BN - 1) / BN;
-  const int n_kv = p.causal ? min(n_kv_all, (q0 + BM - 1) / BN + 1) : n_kv_all;
+  // Heavy causal blocks first: the last query block has the most KV tiles.
+  const int qb = p.causal ? (p.n_qb - 1 - static_cast<int>(blockIdx.x)) : static_cast<int>(blockIdx.x);
+  const int bh = blockIdx.z * p.H + blockIdx.y;
+  const int q0 = qb * BQ;
+  int n_t[QTILES];
+#pragma unroll
+  for (int i = 0; i < QTILES; ++i) n_t[i] = kv_tiles(p, q0 + i * BM);
+  const int n_max = max(n_t[0], n_t[1]);
 
   if (threadIdx.x == 0) {
     mbar_init(&ctl->q_full, 1);
@@ -114,11 +124,13 @@ __global__ void __launch_bounds__(THREADS, 1) fa2_fwd_kernel(const __grid_consta
       mbar_init(&ctl->k_full[s], 1);
       mbar_init(&ctl->v_full[s], 1);
       mbar_init(&ctl->kv_empty[s], 1);
-      mbar_init(&ctl->s_full[s], 1);
-      mbar_init(&ctl->s_free[s], 4);
     }
-    mbar_init(&ctl->p_full, 4);
-    mbar_init(&ctl->o_done, 1);
+    for (int i = 0; i < QTILES; ++i) {
+      mbar_init(&ctl->s_full[i], 1);
+      mbar_init(&ctl->sm_done[i], 4);
+      mbar_init(&ctl->o_ready[i], 4);
+      mbar_init(&ctl->o_final[i], 1);
+    }
     mbar_init(&ctl->drain, 1);
     ctl->abort = 0;
     fence_mbar_init();
@@ -126,7 +138,7 @@ __global__ void __launch_bounds__(THREADS, 1) fa2_fwd_kernel(const __grid_consta
     prefetch_tensormap(&tk);
     prefetch_tensormap(&tv);
   }
-  if (warp == 1) {
+  if (warp == MMA_WARP) {
     tmem_alloc(&ctl->tmem_base, TMEM_COLS);
     tmem_relinquish();
   }
@@ -135,15 +147,18 @@ __global__ void __launch_bounds__(THREADS, 1) fa2_fwd_kernel(const __grid_consta
   tc_fence_after();
   const uint32_t tmem = ctl->tmem_base;
 
-  if (warp == 0) {
+  if (warp == TMA_WARP) {
     // ------------------------------------------------------------------ TMA producer
     if (elect_one_lane()) {
       bool ok = true;
       int issued = 0;
-      mbar_arrive_expect_tx(&ctl->q_full, L::Q_BYTES);
+      mbar_arrive_expect_tx(&ctl->q_full, QTILES * L::Q_BYTES);
 #pragma unroll
-      for (int d = 0; d < D / 64; ++d) tma_load_3d(smem + L::Q_OFF + d * (BM * 128), &tq, &ctl->q_full, d * 64, q0, bh);
-      for (int j = 0; j < n_kv && ok; ++j) {
+      for (int i = 0; i < QTILES; ++i)
+#pragma unroll
+        for (int d = 0; d < D / 64; ++d)
+          tma_load_3d(smem + L::Q_OFF + i * L::Q_BYTES + d * (BM * 128), &tq, &ctl->q_full, d * 64, q0 + i * BM, bh);
+      for (int j = 0; j < n_max && ok; ++j) {
         const int s = j & 1;
         const uint32_t ph = (j >> 1) & 1;
         if (!mbar_wait_bounded(&ctl->kv_empty[s], ph ^ 1, p.wait_limit, abort_flag)) {
@@ -175,170 +190,201 @@ __global__ void __launch_bounds__(THREADS, 1) fa2_fwd_kernel(const __grid_consta
         }
       }
     }
-  } else if (warp == 1) {
+  } else if (warp == MMA_WARP) {
     // ------------------------------------------------------------------ MMA issuer
     if (elect_one_lane()) {
       constexpr uint32_t idesc_s = umma_idesc_f16_f32(BM, BN, 0, 0);  // B = K tile, K-major
       constexpr uint32_t idesc_o = umma_idesc_f16_f32(BM, D, 0, 1);   // B = V tile, N-major
       bool ok = mbar_wait_bounded(&ctl->q_full, 0, p.wait_limit, abort_flag);
       if (!ok && !*abort_flag) fa2_abort(ctl, NTL_STATUS_MMA_FULL_WAIT);
-      const uint32_t q_addr = smem_u32(smem + L::Q_OFF);
-      auto issue_pv = [&](int j) -> bool {
-        const int s = j & 1;
-        if (!mbar_wait_bounded(&ctl->p_full, j & 1, p.wait_limit, abort_flag) ||
-            !mbar_wait_bounded(&ctl->v_full[s], (j >> 1) & 1, p.wait_limit, abort_flag)) {
-          if (!*abort_flag) fa2_abort(ctl, NTL_STATUS_MMA_FULL_WAIT);
-          return false;
-        }
-        tc_fence_after();
-        const uint32_t p_addr = smem_u32(smem + L::P_OFF + (j & 1) * L::P_BYTES);
-        const uint32_t v_addr = smem_u32(smem + L::V_OFF + s * L::KV_BYTES);
-#pragma unroll
-        for (int kk = 0; kk < BN / 16; ++kk) {
-          const uint64_t adesc = umma_desc_sw128(p_addr + (kk >> 2) * (BM * 128) + (kk & 3) * 32, 16, 1024);
-          const uint64_t bdesc = umma_desc_sw128(v_addr + kk * 2048, BN * 128, 1024);
-          tc_mma_f16_ss(tmem + O_COL, adesc, bdesc, idesc_o, (j > 0 || kk > 0) ? 1u : 0u);
-        }
-        tc_commit(&ctl->o_done);
-        tc_commit(&ctl->kv_empty[s]);
-        return true;
+      auto wait_or_abort = [&](uint64_t* bar, uint32_t parity) -> bool {
+        if (mbar_wait_bounded(bar, parity, p.wait_limit, abort_flag)) return true;
+        if (!*abort_flag) fa2_abort(ctl, NTL_STATUS_MMA_FULL_WAIT);
+        return false;
       };
-      for (int j = 0; j < n_kv && ok; ++j) {
-        const int s = j & 1;
-        if (!mbar_wait_bounded(&ctl->k_full[s], (j >> 1) & 1, p.wait_limit, abort_flag) ||
-            (j >= 2 && !mbar_wait_bounded(&ctl->s_free[s], ((j >> 1) & 1) ^ 1, p.wait_limit, abort_flag))) {
-          if (!*abort_flag) fa2_abort(ctl, NTL_STATUS_MMA_FULL_WAIT);
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-        const uint32_t k_addr = smem_u32(smem + L::K_OFF + s * L::KV_BYTES);
+      auto issue_s = [&](int i, int j) {  // S_i = Q_i K_j^T
+        const uint32_t q_addr = smem_u32(smem + L::Q_OFF + i * L::Q_BYTES);
+        const uint32_t k_addr = smem_u32(smem + L::K_OFF + (j & 1) * L::KV_BYTES);
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
           const uint32_t off = (kk >> 2) * (BM * 128) + (kk & 3) * 32;
-          const uint32_t koff = (kk >> 2) * (BN * 128) + (kk & 3) * 32;
-          tc_mma_f16_ss(tmem + S_COL + s * BN, umma_desc_sw128(q_addr + off, 16, 1024),
-                        umma_desc_sw128(k_addr + koff, 16, 1024), idesc_s, kk > 0 ? 1u : 0u);
+          tc_mma_f16_ss(tmem + L::S_COL(i), umma_desc_sw128(q_addr + off, 16, 1024),
+                        umma_desc_sw128(k_addr + off, 16, 1024), idesc_s, kk > 0 ? 1u : 0u);
         }
-        tc_commit(&ctl->s_full[s]);
-        if (j >= 1 && !issue_pv(j - 1)) {
-          ok = false;
-          break;
-        }
+        tc_commit(&ctl->s_full[i]);
+      };
+      if (ok && wait_or_abort(&ctl->k_full[0], 0)) {
+        tc_fence_after();
+        for (int i = 0; i < QTILES; ++i)
+          if (n_t[i] > 0) issue_s(i, 0);
+      } else {
+        ok = false;
       }
-      if (ok) ok = issue_pv(n_kv - 1);
+      for (int j = 0; j < n_max && ok; ++j) {
+        const int s = j & 1;
+        for (int i = 0; i < QTILES && ok; ++i) {
+          if (j >= n_t[i]) continue;
+          if (!wait_or_abort(&ctl->o_ready[i], j & 1) || !wait_or_abort(&ctl->v_full[s], (j >> 1) & 1)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t v_addr = smem_u32(smem + L::V_OFF + s * L::KV_BYTES);
+#pragma unroll
+          for (int kk = 0; kk < BN / 16; ++kk)  // P_i: 8 packed columns per 16 keys
+            tc_mma_f16_ts(tmem + L::O_COL(i), tmem + L::S_COL(i) + kk * 8,
+                          umma_desc_sw128(v_addr + kk * 2048, BN * 128, 1024), idesc_o, (j > 0 || kk > 0) ? 1u : 0u);
+          if (j == n_t[i] - 1) tc_commit(&ctl->o_final[i]);
+          if (j + 1 < n_t[i]) {
+            if (!wait_or_abort(&ctl->k_full[(j + 1) & 1], ((j + 1) >> 1) & 1)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            issue_s(i, j + 1);
+          }
+        }
+        if (ok) tc_commit(&ctl->kv_empty[s]);
+      }
       if (!ok) {
         tc_commit(&ctl->drain);
         if (!mbar_wait_bounded(&ctl->drain, 0, int64_t(1) << 24, nullptr))
           atomicCAS(&g_fa2_status, 0u, NTL_STATUS_DRAIN_WAIT);
       }
     }
-  } else {
+  } else if (warp < 8) {
     // ------------------------------------------------------------------ softmax warps
+    const int i = warp >> 2;     // query tile
     const int quarter = warp & 3;
-    const int r = quarter * 32 + lane;  // row in tile == TMEM lane
-    const int qrow = q0 + r;
+    const int r = quarter * 32 + lane;
+    const int tile_q0 = q0 + i * BM;
+    const int qrow = tile_q0 + r;
     const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
+    const uint32_t s_addr = tmem + lane_off + L::S_COL(i);
     const float c = p.c;
-    float m_old = -INFINITY, l = 0.0f;
-    bool ok = true;
-    for (int j = 0; j < n_kv; ++j) {
-      const int s = j & 1;
+    float m_use = -INFINITY, l = 0.0f;
+    for (int j = 0; j < n_t[i]; ++j) {
       const int k0 = j * BN;
-      if (!mbar_wait_bounded(&ctl->s_full[s], (j >> 1) & 1, p.wait_limit, abort_flag)) {
+      if (!mbar_wait_bounded(&ctl->s_full[i], j & 1, p.wait_limit, abort_flag)) {
         if (!*abort_flag) fa2_abort(ctl, NTL_STATUS_SOFTMAX_WAIT);
-        ok = false;
         break;
       }
       __syncwarp();
       tc_fence_after();
-      const uint32_t s_addr = tmem + lane_off + S_COL + s * BN;
-      const bool masked_tile = (k0 + BN > p.S) || (p.causal && k0 + BN - 1 > q0);
-      // pass 1: row max
+      const bool masked_tile = (k0 + BN > p.S) || (p.causal && k0 + BN - 1 > tile_q0);
+      const int key_lim = p.causal ? min(p.S, qrow + 1) : p.S;  // keys < key_lim are kept
       float mx = -INFINITY;
 #pragma unroll
       for (int ch = 0; ch < BN / 32; ++ch) {
-        uint32_t v[32];
-        tmem_ld_32x32b_x32(s_addr + ch * 32, v);
+        uint32_t a[32];
+        tmem_ld_32x32b_x32(s_addr + ch * 32, a);
         tc_wait_ld();
+        if (masked_tile) {
 #pragma unroll
-        for (int e = 0; e < 32; ++e) {
-          const int key = k0 + ch * 32 + e;
-          const bool keep = !masked_tile || (key < p.S && (!p.causal || key <= qrow));
-          mx = fmaxf(mx, keep ? __uint_as_float(v[e]) : -INFINITY);
+          for (int e = 0; e < 32; ++e) mx = fmaxf(mx, k0 + ch * 32 + e < key_lim ? __uint_as_float(a[e]) : -INFINITY);
+        } else {
+#pragma unroll
+          for (int e = 0; e < 32; ++e) mx = fmaxf(mx, __uint_as_float(a[e]));
         }
       }
-      const float m_new = fmaxf(m_old, mx);
-      const float mc = m_new * c;
-      // pass 2: p = exp2(s*c - m*c) -> fp16 P tile (row r), running sum
+      const float m_new = fmaxf(m_use, mx);
+      bool rescale = false;
+      float rs = 1.0f;
+      if (j == 0) {
+        m_use = m_new;
+      } else if ((m_new - m_use) * c > kRescaleLog2) {
+        rs = ex2_approx((m_use - m_new) * c);
+        m_use = m_new;
+        rescale = true;
+      }
+      const float mc = m_use * c;
       float sum = 0.0f;
-      const uint32_t p_base = smem_u32(smem + L::P_OFF + s * L::P_BYTES);
-#pragma unroll
+#pragma unroll 1
       for (int ch = 0; ch < BN / 32; ++ch) {
-        uint32_t v[32];
-        tmem_ld_32x32b_x32(s_addr + ch * 32, v);
+        uint32_t a[32];
+        tmem_ld_32x32b_x32(s_addr + ch * 32, a);
         tc_wait_ld();
-        float pv[32];
+        uint32_t pk[16];
+        float part = 0.0f;
 #pragma unroll
-        for (int e = 0; e < 32; ++e) {
-          const int key = k0 + ch * 32 + e;
-          const bool keep = !masked_tile || (key < p.S && (!p.causal || key <= qrow));
-          pv[e] = keep ? exp2f(__fmaf_rn(__uint_as_float(v[e]), c, -mc)) : 0.0f;
-          sum += pv[e];
+        for (int e = 0; e < 16; ++e) {
+          const int ka = k0 + ch * 32 + 2 * e;
+          float p0 = ex2_approx(__fmaf_rn(__uint_as_float(a[2 * e]), c, -mc));
+          float p1 = ex2_approx(__fmaf_rn(__uint_as_float(a[2 * e + 1]), c, -mc));
+          if (masked_tile) {
+            p0 = ka < key_lim ? p0 : 0.0f;
+            p1 = ka + 1 < key_lim ? p1 : 0.0f;
+          }
+          part += p0 + p1;
+          pk[e] = pack_half2(p0, p1);
         }
-        // 32 keys = 4 chunks of 8 halves; keys [64a, 64a+64) live in atom column a.
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          const int key_chunk = ch * 4 + q;  // 0..15 chunks of 8 keys
-          const uint32_t addr = p_base + (key_chunk >> 3) * (BM * 128) + sw128_offset(r, key_chunk & 7);
-          st_shared_v4(addr, pack_half2(pv[q * 8 + 0], pv[q * 8 + 1]), pack_half2(pv[q * 8 + 2], pv[q * 8 + 3]),
-                       pack_half2(pv[q * 8 + 4], pv[q * 8 + 5]), pack_half2(pv[q * 8 + 6], pv[q * 8 + 7]));
-        }
+        sum += part;
+        // P keys [32*ch, 32*ch + 32) -> packed columns [16*ch, 16*ch + 16) of S_i (already read).
+        tmem_st_32x32b_x16(s_addr + ch * 16, pk);
       }
-      // S buffer s may now be overwritten by S_{j+2}.
+      l = (j == 0) ? sum : __fmaf_rn(l, rs, sum);
+      ctl->scale[i][r] = rs;  // 1.0 for rows whose max did not move
+      const bool any = __any_sync(0xffffffffu, rescale);
+      if (lane == 0) ctl->need[i][quarter] = any ? 1 : 0;
+      if (j == n_t[i] - 1) ctl->lsum[i][r] = l;
+      tc_wait_st();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&ctl->s_free[s]);
-      const float rscale = (j == 0) ? 0.0f : exp2f(m_old * c - mc);
-      l = (j == 0) ? sum : __fmaf_rn(l, rscale, sum);
-      if (j > 0) {
-        // O holds P_{<j} V; rescale it once P_{j-1} V_{j-1} has retired.
-        if (!mbar_wait_bounded(&ctl->o_done, (j - 1) & 1, p.wait_limit, abort_flag)) {
+      if (lane == 0) mbar_arrive(&ctl->sm_done[i]);
+    }
+  } else if (warp < 12) {
+    // ------------------------------------------------------------------ correction + epilogue
+    const int quarter = warp & 3;
+    const int r = quarter * 32 + lane;
+    const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
+    bool ok = true;
+    for (int j = 0; j < n_max && ok; ++j) {
+      for (int i = 0; i < QTILES; ++i) {
+        if (j >= n_t[i]) continue;
+        if (!mbar_wait_bounded(&ctl->sm_done[i], j & 1, p.wait_limit, abort_flag)) {
           if (!*abort_flag) fa2_abort(ctl, NTL_STATUS_SOFTMAX_WAIT);
           ok = false;
           break;
         }
         __syncwarp();
-        tc_fence_after();
-        if (__any_sync(0xffffffffu, rscale != 1.0f)) {
+        if (j > 0 && *reinterpret_cast<volatile int*>(&ctl->need[i][quarter])) {
+          tc_fence_after();
+          const float rs = ctl->scale[i][r];
+          const bool mine = rs != 1.0f;
 #pragma unroll
           for (int ch = 0; ch < D / 16; ++ch) {
             uint32_t o[16];
-            tmem_ld_32x32b_x16(tmem + lane_off + O_COL + ch * 16, o);
+            const uint32_t addr = tmem + lane_off + L::O_COL(i) + ch * 16;
+            tmem_ld_32x32b_x16(addr, o);
             tc_wait_ld();
+            if (mine) {
 #pragma unroll
-            for (int e = 0; e < 16; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * rscale);
-            tmem_st_32x32b_x16(tmem + lane_off + O_COL + ch * 16, o);
+              for (int e = 0; e < 16; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * rs);
+            }
+            tmem_st_32x32b_x16(addr, o);
           }
           tc_wait_st();
         }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&ctl->o_ready[i]);
       }
-      fence_proxy_async_smem();  // P (generic-proxy stores) -> visible to the tensor core
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&ctl->p_full);
-      m_old = m_new;
     }
-    // epilogue: O / l -> fp16
-    if (ok && mbar_wait_bounded(&ctl->o_done, (n_kv - 1) & 1, p.wait_limit, abort_flag)) {
+    for (int i = 0; i < QTILES && ok; ++i) {
+      if (n_t[i] == 0) continue;
+      if (!mbar_wait_bounded(&ctl->o_final[i], 0, p.wait_limit, abort_flag)) {
+        if (!*abort_flag) fa2_abort(ctl, NTL_STATUS_SOFTMAX_WAIT);
+        break;
+      }
       __syncwarp();
       tc_fence_after();
-      const float inv_l = 1.0f / l;
+      const int qrow = q0 + i * BM + r;
+      const float inv_l = 1.0f / ctl->lsum[i][r];
       __half* orow = p.o + (static_cast<int64_t>(bh) * p.S + qrow) * D;
 #pragma unroll
       for (int ch = 0; ch < D / 16; ++ch) {
         uint32_t o[16];
-        tmem_ld_32x32b_x16(tmem + lane_off + O_COL + ch * 16, o);
+        tmem_ld_32x32b_x16(tmem + lane_off + L::O_COL(i) + ch * 16, o);
         tc_wait_ld();
         if (qrow < p.S) {
           uint32_t h[8];
@@ -350,15 +396,13 @@ __global__ void __launch_bounds__(THREADS, 1) fa2_fwd_kernel(const __grid_consta
           dst[1] = make_uint4(h[4], h[5], h[6], h[7]);
         }
       }
-    } else if (ok && !*abort_flag) {
-      fa2_abort(ctl, NTL_STATUS_SOFTMAX_WAIT);
     }
   }
 
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  if (warp == 1) tmem_dealloc(tmem, TMEM_COLS);
+  if (warp == MMA_WARP) tmem_dealloc(tmem, TMEM_COLS);
 }
 
 // ------------------------------------------------------------------------- host side
@@ -408,7 +452,7 @@ int launch_fa2(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& 
     if (e != cudaSuccess) return ntl_fail(NTL_ERR_CUDA, "cudaFuncSetAttribute(fa2): %s", cudaGetErrorString(e));
     done_mask.fetch_or(bit, std::memory_order_release);
   }
-  dim3 grid(static_cast<unsigned>(p.n_qt), static_cast<unsigned>(heads), static_cast<unsigned>(batch));
+  dim3 grid(static_cast<unsigned>(p.n_qb), static_cast<unsigned>(heads), static_cast<unsigned>(batch));
   fa2_fwd_kernel<D><<<grid, THREADS, Fa2Smem<D>::BYTES, s>>>(mq, mk, mv, p);
   ntl_note_launch();
   return ntl_check_launch("attention launch");
@@ -447,7 +491,7 @@ extern "C" int ntl_fa2_fwd_f16(const uint16_t* q, const uint16_t* k, const uint1
   p.o = reinterpret_cast<__half*>(o);
   p.S = static_cast<int>(seq);
   p.H = static_cast<int>(heads);
-  p.n_qt = static_cast<int>((seq + BM - 1) / BM);
+  p.n_qb = static_cast<int>((seq + BQ - 1) / BQ);
   p.causal = causal ? 1 : 0;
   p.c = scale_log2;
   p.wait_limit = ntl_wait_limit();
