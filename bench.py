@@ -540,8 +540,22 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--ops", default=",".join(OPS))
-    ap.add_argument("--cpu-seconds", type=float, default=2.0)
+    ap.add_argument("--cpu-seconds", type=float, default=2.0, help="CPU-baseline sample per op (0 = skip)")
+    ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer end-to-end leg")
+    ap.add_argument("--gemm-shape", default=None, help="M,N,K override (profiling a small case)")
+    ap.add_argument("--fa2-shape", default=None, help="B,H,S,D override (profiling a small case)")
     args = ap.parse_args()
+    if args.gemm_shape:
+        m, n, k = (int(x) for x in args.gemm_shape.split(","))
+        for cls in (GemmOp, GemmBiasReluOp):
+            cls.m, cls.n, cls.k = m, n, k
+            cls.config = cls.config + f" [override M,N,K={m},{n},{k}]"
+    if args.fa2_shape:
+        b, h, s_, d = (int(x) for x in args.fa2_shape.split(","))
+        for cls in (FA2Op, FA2CausalOp):
+            cls.B, cls.H, cls.S, cls.D = b, h, s_, d
+            cls.config = cls.config + f" [override B,H,S,D={b},{h},{s_},{d}]"
+
     ops = [o for o in args.ops.split(",") if o]
     for o in ops:
         if o not in OPS:
@@ -626,14 +640,14 @@ def run_ours(args, ops):
         op = OPS[name](torch, device, rank)
         try:
             results[name] = run_op(op, torch, dist, world, args.steps, args.warmup, stream, peaks, peak_kind, traffic,
-                                   want_e2e=True)
+                                   want_e2e=not args.no_e2e)
         except _lib.KernelError as exc:
             if exc.code != 2:
                 raise
             results[name] = {"unavailable": str(exc)}
             op.sets = None
     clocks = sampler.stop()
-    if rank == 0 and world == 1:
+    if rank == 0 and world == 1 and args.cpu_seconds > 0:
         for name in ops:
             if "unavailable" not in results[name]:
                 results[name]["cpu_baseline"] = cpu_baseline(OPS[name](None, None, 0), args.cpu_seconds)
@@ -653,7 +667,7 @@ def run_ours(args, ops):
                    "parallelism": f"row-sharded x{world}, no collective" if world > 1 else "single GPU",
                    "l2": "inputs rotated over buffer sets larger than L2 between reuses",
                    "timing": "K launches replayed from one CUDA graph, CUDA events, max over ranks"},
-        "roofline": head["roofline"], "e2e": head["e2e"], "gpu_launches": total_launches, "clocks": clocks,
+        "roofline": head["roofline"], "e2e": head.get("e2e"), "gpu_launches": total_launches, "clocks": clocks,
         "cpu_baseline": head.get("cpu_baseline"), "ops": results,
     }
     print(json.dumps(line), flush=True)

@@ -7,20 +7,20 @@
 // statistics (codegen.py:972-984, :1062-1073).
 //
 // Design: one CTA = one (batch, head, 256-query block) = two 128-row query tiles that
-// share every K/V tile (448 threads, 14 warps):
-//   warps 0-3   softmax of query tile 0, one row per thread (TMEM lane = row)
-//   warps 4-7   softmax of query tile 1
-//   warps 8-11  O correction (rescale in TMEM when a row max moved) and the final
-//               O / l -> fp16 epilogue of both tiles
-//   warp 12     TMEM owner (512 columns: S0, S1, O0, O1) and MMA issuer
-//   warp 13     TMA: Q0, Q1 once, then K_j / V_j (128 keys x D) into a 2-stage ring; 3-D
+// share every K/V tile (320 threads, 10 warps):
+//   warps 0-3   softmax, O rescale and the O / l -> fp16 epilogue of query tile 0, one row
+//               per thread (TMEM lane = row)
+//   warps 4-7   the same for query tile 1
+//   warp 8      TMEM owner (512 columns: S0, S1, O0, O1) and MMA issuer
+//   warp 9      TMA: Q0, Q1 once, then K_j / V_j (128 keys x D) into a 2-stage ring; 3-D
 //               tensor maps [B*H, S, D] zero-fill rows past S and never cross heads.
 // Per KV tile j the MMA warp issues, per query tile i: O_i += P_i V_j (A = P_i from TMEM,
 // fp16 packed in place over S_i; B = V_j N-major in smem) and then S_i = Q_i K_{j+1}^T
 // (both operands K-major in smem), so the tensor core works on one tile while the other
 // tile's softmax runs.  Softmax uses a lazily updated row max: O and l are rescaled only
-// when the max grows by more than 2^8 (P stays <= 256, exact in the final O / l), and the
-// rescale itself runs in the correction warps.  Masked scores (causal key > query, keys
+// when the max grows by more than 2^8 (P stays <= 256, exact in the final O / l).  S_i of
+// tile j is issued after P_i V_{j-1}, so once S_i is ready O_i is stable and the softmax
+// warps rescale it in place without another hand-off.  Masked scores (causal key > query, keys
 // >= S) contribute exactly 0, like the reference's -1e30 fill.  Every mbarrier wait is
 // bounded; a wait that gives up records a status code, drains in-flight copies and
 // MMAs, frees TMEM and returns.
@@ -37,8 +37,8 @@ constexpr int BM = 128;        // rows per query tile
 constexpr int QTILES = 2;      // query tiles per CTA
 constexpr int BQ = BM * QTILES;
 constexpr int BN = 128;        // keys per KV tile
-constexpr int THREADS = 448;
-constexpr int MMA_WARP = 12, TMA_WARP = 13;
+constexpr int THREADS = 320;
+constexpr int MMA_WARP = 8, TMA_WARP = 9;
 constexpr uint32_t TMEM_COLS = 512;
 constexpr float kRescaleLog2 = 8.0f;  // lazy-rescale threshold (log2 units)
 
@@ -55,14 +55,10 @@ struct __align__(16) Fa2Ctl {
   uint64_t k_full[2], v_full[2], kv_empty[2];
   uint64_t s_full[QTILES];
   uint64_t sm_done[QTILES];
-  uint64_t o_ready[QTILES];
   uint64_t o_final[QTILES];
   uint64_t drain;
   uint32_t tmem_base;
   int abort;
-  int need[QTILES][4];
-  float scale[QTILES][BM];
-  float lsum[QTILES][BM];
 };
 
 template <int D>
@@ -88,6 +84,24 @@ __device__ __forceinline__ void fa2_abort(Fa2Ctl* ctl, uint32_t code) {
 __device__ __forceinline__ uint32_t pack_half2(float a, float b) {
   __half2 h = __floats2half2_rn(a, b);
   return *reinterpret_cast<uint32_t*>(&h);
+}
+
+// 2^x on the FMA pipe, for x <= ~8 (softmax exponents): x = n + f with n = round(x) via
+// the 1.5*2^23 rounding constant, 2^f on [-1/2, 1/2] by a cubic fitted here for minimum
+// relative error (max 7.6e-5, below fp16's half-ulp 2.4e-4 that P is rounded to), and
+// 2^n added to the exponent bits.  x is clamped at -126 so the exponent never underflows;
+// such terms (masked or tiny scores) become ~1e-38, i.e. 0 in fp16 P.  Used for a fixed
+// quarter of the exponentials so the MUFU ex2 unit and the FMA pipe share the load.
+__device__ __forceinline__ float exp2_fma(float x) {
+  constexpr float kRound = 12582912.0f;  // 1.5 * 2^23
+  x = fmaxf(x, -126.0f);
+  const float t = __fadd_rn(x, kRound);
+  const float n = __fsub_rn(t, kRound);
+  const float f = __fsub_rn(x, n);
+  float q = __fmaf_rn(0.055170975625514984f, f, 0.24260970950126648f);
+  q = __fmaf_rn(q, f, 0.6932609677314758f);
+  q = __fmaf_rn(q, f, 0.9999281764030457f);
+  return __uint_as_float(__float_as_uint(q) + (__float_as_uint(t) << 23));
 }
 
 // Number of KV tiles query tile i of block qb needs (0 when the tile is past S).
@@ -128,7 +142,6 @@ __global__ void __launch_bounds__(THREADS, 1) fa2_fwd_kernel(const __grid_consta
     for (int i = 0; i < QTILES; ++i) {
       mbar_init(&ctl->s_full[i], 1);
       mbar_init(&ctl->sm_done[i], 4);
-      mbar_init(&ctl->o_ready[i], 4);
       mbar_init(&ctl->o_final[i], 1);
     }
     mbar_init(&ctl->drain, 1);
@@ -224,7 +237,7 @@ __global__ void __launch_bounds__(THREADS, 1) fa2_fwd_kernel(const __grid_consta
         const int s = j & 1;
         for (int i = 0; i < QTILES && ok; ++i) {
           if (j >= n_t[i]) continue;
-          if (!wait_or_abort(&ctl->o_ready[i], j & 1) || !wait_or_abort(&ctl->v_full[s], (j >> 1) & 1)) {
+          if (!wait_or_abort(&ctl->sm_done[i], j & 1) || !wait_or_abort(&ctl->v_full[s], (j >> 1) & 1)) {
             ok = false;
             break;
           }
@@ -254,42 +267,47 @@ __global__ void __launch_bounds__(THREADS, 1) fa2_fwd_kernel(const __grid_consta
     }
   } else if (warp < 8) {
     // ------------------------------------------------------------------ softmax warps
-    const int i = warp >> 2;     // query tile
+    const int i = warp >> 2;  // query tile
     const int quarter = warp & 3;
     const int r = quarter * 32 + lane;
     const int tile_q0 = q0 + i * BM;
     const int qrow = tile_q0 + r;
     const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
     const uint32_t s_addr = tmem + lane_off + L::S_COL(i);
+    const uint32_t o_addr = tmem + lane_off + L::O_COL(i);
     const float c = p.c;
+    const int key_lim = p.causal ? min(p.S, qrow + 1) : p.S;  // keys < key_lim are kept
     float m_use = -INFINITY, l = 0.0f;
+    bool ok = true;
     for (int j = 0; j < n_t[i]; ++j) {
       const int k0 = j * BN;
       if (!mbar_wait_bounded(&ctl->s_full[i], j & 1, p.wait_limit, abort_flag)) {
         if (!*abort_flag) fa2_abort(ctl, NTL_STATUS_SOFTMAX_WAIT);
+        ok = false;
         break;
       }
       __syncwarp();
       tc_fence_after();
       const bool masked_tile = (k0 + BN > p.S) || (p.causal && k0 + BN - 1 > tile_q0);
-      const int key_lim = p.causal ? min(p.S, qrow + 1) : p.S;  // keys < key_lim are kept
-      float mx = -INFINITY;
+      uint32_t v[BN];
 #pragma unroll
-      for (int ch = 0; ch < BN / 32; ++ch) {
-        uint32_t a[32];
-        tmem_ld_32x32b_x32(s_addr + ch * 32, a);
-        tc_wait_ld();
-        if (masked_tile) {
+      for (int ch = 0; ch < BN / 32; ++ch) tmem_ld_32x32b_x32(s_addr + ch * 32, *reinterpret_cast<uint32_t(*)[32]>(v + ch * 32));
+      tc_wait_ld();
+      if (masked_tile) {
 #pragma unroll
-          for (int e = 0; e < 32; ++e) mx = fmaxf(mx, k0 + ch * 32 + e < key_lim ? __uint_as_float(a[e]) : -INFINITY);
-        } else {
-#pragma unroll
-          for (int e = 0; e < 32; ++e) mx = fmaxf(mx, __uint_as_float(a[e]));
-        }
+        for (int e = 0; e < BN; ++e)
+          if (k0 + e >= key_lim) v[e] = __float_as_uint(-INFINITY);
       }
+      // Row max with 8 independent partial maxima (a short dependency chain).
+      float pm[8];
+#pragma unroll
+      for (int a = 0; a < 8; ++a) pm[a] = __uint_as_float(v[a]);
+#pragma unroll
+      for (int e = 8; e < BN; ++e) pm[e & 7] = fmaxf(pm[e & 7], __uint_as_float(v[e]));
+      const float mx = fmaxf(fmaxf(fmaxf(pm[0], pm[1]), fmaxf(pm[2], pm[3])), fmaxf(fmaxf(pm[4], pm[5]), fmaxf(pm[6], pm[7])));
       const float m_new = fmaxf(m_use, mx);
-      bool rescale = false;
       float rs = 1.0f;
+      bool rescale = false;
       if (j == 0) {
         m_use = m_new;
       } else if ((m_new - m_use) * c > kRescaleLog2) {
@@ -297,103 +315,67 @@ __global__ void __launch_bounds__(THREADS, 1) fa2_fwd_kernel(const __grid_consta
         m_use = m_new;
         rescale = true;
       }
-      const float mc = m_use * c;
-      float sum = 0.0f;
+      if (__any_sync(0xffffffffu, rescale)) {
+        // O_i = P_{<j} V is complete: S_i of this tile was issued after the last P_i V.
 #pragma unroll 1
+        for (int ch = 0; ch < D / 16; ++ch) {
+          uint32_t o[16];
+          tmem_ld_32x32b_x16(o_addr + ch * 16, o);
+          tc_wait_ld();
+#pragma unroll
+          for (int e = 0; e < 16; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * rs);
+          tmem_st_32x32b_x16(o_addr + ch * 16, o);
+        }
+      }
+      const float mc = m_use * c;
+      float ps[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};  // independent partial sums
+#pragma unroll
       for (int ch = 0; ch < BN / 32; ++ch) {
-        uint32_t a[32];
-        tmem_ld_32x32b_x32(s_addr + ch * 32, a);
-        tc_wait_ld();
         uint32_t pk[16];
-        float part = 0.0f;
 #pragma unroll
         for (int e = 0; e < 16; ++e) {
-          const int ka = k0 + ch * 32 + 2 * e;
-          float p0 = ex2_approx(__fmaf_rn(__uint_as_float(a[2 * e]), c, -mc));
-          float p1 = ex2_approx(__fmaf_rn(__uint_as_float(a[2 * e + 1]), c, -mc));
-          if (masked_tile) {
-            p0 = ka < key_lim ? p0 : 0.0f;
-            p1 = ka + 1 < key_lim ? p1 : 0.0f;
-          }
-          part += p0 + p1;
+          // masked scores are -inf: exp2 gives exactly 0
+          const float x0 = __fmaf_rn(__uint_as_float(v[ch * 32 + 2 * e]), c, -mc);
+          const float x1 = __fmaf_rn(__uint_as_float(v[ch * 32 + 2 * e + 1]), c, -mc);
+          const bool on_fma = (e & 3) == 3;  // a fixed quarter of the pairs
+          const float p0 = on_fma ? exp2_fma(x0) : ex2_approx(x0);
+          const float p1 = on_fma ? exp2_fma(x1) : ex2_approx(x1);
+          ps[e & 7] += p0 + p1;
           pk[e] = pack_half2(p0, p1);
         }
-        sum += part;
-        // P keys [32*ch, 32*ch + 32) -> packed columns [16*ch, 16*ch + 16) of S_i (already read).
+        // P keys [32*ch, 32*ch + 32) -> packed columns [16*ch, 16*ch + 16) of S_i (S is in registers).
         tmem_st_32x32b_x16(s_addr + ch * 16, pk);
       }
+      const float sum = ((ps[0] + ps[1]) + (ps[2] + ps[3])) + ((ps[4] + ps[5]) + (ps[6] + ps[7]));
       l = (j == 0) ? sum : __fmaf_rn(l, rs, sum);
-      ctl->scale[i][r] = rs;  // 1.0 for rows whose max did not move
-      const bool any = __any_sync(0xffffffffu, rescale);
-      if (lane == 0) ctl->need[i][quarter] = any ? 1 : 0;
-      if (j == n_t[i] - 1) ctl->lsum[i][r] = l;
       tc_wait_st();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&ctl->sm_done[i]);
     }
-  } else if (warp < 12) {
-    // ------------------------------------------------------------------ correction + epilogue
-    const int quarter = warp & 3;
-    const int r = quarter * 32 + lane;
-    const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
-    bool ok = true;
-    for (int j = 0; j < n_max && ok; ++j) {
-      for (int i = 0; i < QTILES; ++i) {
-        if (j >= n_t[i]) continue;
-        if (!mbar_wait_bounded(&ctl->sm_done[i], j & 1, p.wait_limit, abort_flag)) {
-          if (!*abort_flag) fa2_abort(ctl, NTL_STATUS_SOFTMAX_WAIT);
-          ok = false;
-          break;
-        }
-        __syncwarp();
-        if (j > 0 && *reinterpret_cast<volatile int*>(&ctl->need[i][quarter])) {
-          tc_fence_after();
-          const float rs = ctl->scale[i][r];
-          const bool mine = rs != 1.0f;
-#pragma unroll
-          for (int ch = 0; ch < D / 16; ++ch) {
-            uint32_t o[16];
-            const uint32_t addr = tmem + lane_off + L::O_COL(i) + ch * 16;
-            tmem_ld_32x32b_x16(addr, o);
-            tc_wait_ld();
-            if (mine) {
-#pragma unroll
-              for (int e = 0; e < 16; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * rs);
-            }
-            tmem_st_32x32b_x16(addr, o);
-          }
-          tc_wait_st();
-        }
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&ctl->o_ready[i]);
-      }
-    }
-    for (int i = 0; i < QTILES && ok; ++i) {
-      if (n_t[i] == 0) continue;
+    // epilogue: O / l -> fp16
+    if (ok && n_t[i] > 0) {
       if (!mbar_wait_bounded(&ctl->o_final[i], 0, p.wait_limit, abort_flag)) {
         if (!*abort_flag) fa2_abort(ctl, NTL_STATUS_SOFTMAX_WAIT);
-        break;
-      }
-      __syncwarp();
-      tc_fence_after();
-      const int qrow = q0 + i * BM + r;
-      const float inv_l = 1.0f / ctl->lsum[i][r];
-      __half* orow = p.o + (static_cast<int64_t>(bh) * p.S + qrow) * D;
+      } else {
+        __syncwarp();
+        tc_fence_after();
+        const float inv_l = 1.0f / l;
+        __half* orow = p.o + (static_cast<int64_t>(bh) * p.S + qrow) * D;
+#pragma unroll 1
+        for (int ch = 0; ch < D / 16; ++ch) {
+          uint32_t o[16];
+          tmem_ld_32x32b_x16(o_addr + ch * 16, o);
+          tc_wait_ld();
+          if (qrow < p.S) {
+            uint32_t h[8];
 #pragma unroll
-      for (int ch = 0; ch < D / 16; ++ch) {
-        uint32_t o[16];
-        tmem_ld_32x32b_x16(tmem + lane_off + L::O_COL(i) + ch * 16, o);
-        tc_wait_ld();
-        if (qrow < p.S) {
-          uint32_t h[8];
-#pragma unroll
-          for (int e = 0; e < 8; ++e)
-            h[e] = pack_half2(__uint_as_float(o[2 * e]) * inv_l, __uint_as_float(o[2 * e + 1]) * inv_l);
-          uint4* dst = reinterpret_cast<uint4*>(orow + ch * 16);
-          dst[0] = make_uint4(h[0], h[1], h[2], h[3]);
-          dst[1] = make_uint4(h[4], h[5], h[6], h[7]);
+            for (int e = 0; e < 8; ++e)
+              h[e] = pack_half2(__uint_as_float(o[2 * e]) * inv_l, __uint_as_float(o[2 * e + 1]) * inv_l);
+            uint4* dst = reinterpret_cast<uint4*>(orow + ch * 16);
+            dst[0] = make_uint4(h[0], h[1], h[2], h[3]);
+            dst[1] = make_uint4(h[4], h[5], h[6], h[7]);
+          }
         }
       }
     }
