@@ -12,7 +12,8 @@
 //               per thread (TMEM lane = row)
 //   warps 4-7   the same for query tile 1
 //   warp 8      TMEM owner (512 columns: S0, S1, O0, O1) and MMA issuer
-//   warp 9      TMA: Q0, Q1 once, then K_j / V_j (128 keys x D) into a 2-stage ring; 3-D
+//   warp 9      TMA: Q0, Q1 once, then K_j (3-stage ring, released once both tiles' QK^T
+//               consumed it) and V_j (2-stage ring) with K running one tile ahead; 3-D
 //               tensor maps [B*H, S, D] zero-fill rows past S and never cross heads.
 // Per KV tile j the MMA warp issues, per query tile i: O_i += P_i V_j (A = P_i from TMEM,
 // fp16 packed in place over S_i; B = V_j N-major in smem) and then S_i = Q_i K_{j+1}^T
@@ -37,8 +38,10 @@ constexpr int BM = 128;        // rows per query tile
 constexpr int QTILES = 2;      // query tiles per CTA
 constexpr int BQ = BM * QTILES;
 constexpr int BN = 128;        // keys per KV tile
-constexpr int THREADS = 320;
-constexpr int MMA_WARP = 8, TMA_WARP = 9;
+constexpr int KSTAGES = 2, VSTAGES = 2;
+constexpr int THREADS = 576;
+constexpr int MMA_WARP = 16, TMA_WARP = 17;
+constexpr int SM_WARPS_PER_TILE = 8;  // two threads per query row (64 keys each)
 constexpr uint32_t TMEM_COLS = 512;
 constexpr float kRescaleLog2 = 8.0f;  // lazy-rescale threshold (log2 units)
 
@@ -52,13 +55,15 @@ struct Fa2Params {
 
 struct __align__(16) Fa2Ctl {
   uint64_t q_full;
-  uint64_t k_full[2], v_full[2], kv_empty[2];
+  uint64_t k_full[KSTAGES], k_empty[KSTAGES], v_full[VSTAGES], v_empty[VSTAGES];
   uint64_t s_full[QTILES];
   uint64_t sm_done[QTILES];
   uint64_t o_final[QTILES];
+  uint64_t pair[QTILES][4];  // the two half-row warps of (tile, lane quarter)
   uint64_t drain;
   uint32_t tmem_base;
   int abort;
+  float xmax[QTILES][2][BM];  // per-half row maxima, then per-half row sums
 };
 
 template <int D>
@@ -67,8 +72,8 @@ struct Fa2Smem {
   static constexpr int KV_BYTES = BN * D * 2;
   static constexpr int Q_OFF = 0;
   static constexpr int K_OFF = Q_OFF + QTILES * Q_BYTES;
-  static constexpr int V_OFF = K_OFF + 2 * KV_BYTES;
-  static constexpr int CTL_OFF = V_OFF + 2 * KV_BYTES;
+  static constexpr int V_OFF = K_OFF + KSTAGES * KV_BYTES;
+  static constexpr int CTL_OFF = V_OFF + VSTAGES * KV_BYTES;
   static constexpr int USED = CTL_OFF + static_cast<int>(sizeof(Fa2Ctl));
   // >= 116 KB keeps one CTA per SM, so the 512-column TMEM allocation never contends.
   static constexpr int BYTES = (USED + 1024 > 118784 ? USED + 1024 : 118784);
@@ -92,16 +97,24 @@ __device__ __forceinline__ uint32_t pack_half2(float a, float b) {
 // 2^n added to the exponent bits.  x is clamped at -126 so the exponent never underflows;
 // such terms (masked or tiny scores) become ~1e-38, i.e. 0 in fp16 P.  Used for a fixed
 // quarter of the exponentials so the MUFU ex2 unit and the FMA pipe share the load.
-__device__ __forceinline__ float exp2_fma(float x) {
-  constexpr float kRound = 12582912.0f;  // 1.5 * 2^23
-  x = fmaxf(x, -126.0f);
-  const float t = __fadd_rn(x, kRound);
-  const float n = __fsub_rn(t, kRound);
-  const float f = __fsub_rn(x, n);
-  float q = __fmaf_rn(0.055170975625514984f, f, 0.24260970950126648f);
-  q = __fmaf_rn(q, f, 0.6932609677314758f);
-  q = __fmaf_rn(q, f, 0.9999281764030457f);
-  return __uint_as_float(__float_as_uint(q) + (__float_as_uint(t) << 23));
+// Two values per call, with f32x2 arithmetic.
+__device__ __forceinline__ void exp2_fma2(uint64_t x2, float& p0, float& p1) {
+  constexpr float kRound = 12582912.0f;
+  float x0, x1;
+  f2_split(x2, x0, x1);
+  x2 = f2_make(fmaxf(x0, -126.0f), fmaxf(x1, -126.0f));
+  const uint64_t round2 = f2_make(kRound, kRound);
+  const uint64_t t2 = f2_add(x2, round2);
+  const uint64_t f2 = f2_sub(x2, f2_sub(t2, round2));
+  uint64_t q2 = f2_fma(f2_make(0.055170975625514984f, 0.055170975625514984f), f2,
+                       f2_make(0.24260970950126648f, 0.24260970950126648f));
+  q2 = f2_fma(q2, f2, f2_make(0.6932609677314758f, 0.6932609677314758f));
+  q2 = f2_fma(q2, f2, f2_make(0.9999281764030457f, 0.9999281764030457f));
+  float q0, q1, t0, t1;
+  f2_split(q2, q0, q1);
+  f2_split(t2, t0, t1);
+  p0 = __uint_as_float(__float_as_uint(q0) + (__float_as_uint(t0) << 23));
+  p1 = __uint_as_float(__float_as_uint(q1) + (__float_as_uint(t1) << 23));
 }
 
 // Number of KV tiles query tile i of block qb needs (0 when the tile is past S).
@@ -134,15 +147,19 @@ __global__ void __launch_bounds__(THREADS, 1) fa2_fwd_kernel(const __grid_consta
 
   if (threadIdx.x == 0) {
     mbar_init(&ctl->q_full, 1);
-    for (int s = 0; s < 2; ++s) {
+    for (int s = 0; s < KSTAGES; ++s) {
       mbar_init(&ctl->k_full[s], 1);
+      mbar_init(&ctl->k_empty[s], 1);
+    }
+    for (int s = 0; s < VSTAGES; ++s) {
       mbar_init(&ctl->v_full[s], 1);
-      mbar_init(&ctl->kv_empty[s], 1);
+      mbar_init(&ctl->v_empty[s], 1);
     }
     for (int i = 0; i < QTILES; ++i) {
       mbar_init(&ctl->s_full[i], 1);
-      mbar_init(&ctl->sm_done[i], 4);
+      mbar_init(&ctl->sm_done[i], SM_WARPS_PER_TILE);
       mbar_init(&ctl->o_final[i], 1);
+      for (int q = 0; q < 4; ++q) mbar_init(&ctl->pair[i][q], 2);
     }
     mbar_init(&ctl->drain, 1);
     ctl->abort = 0;
@@ -164,43 +181,50 @@ __global__ void __launch_bounds__(THREADS, 1) fa2_fwd_kernel(const __grid_consta
     // ------------------------------------------------------------------ TMA producer
     if (elect_one_lane()) {
       bool ok = true;
-      int issued = 0;
       mbar_arrive_expect_tx(&ctl->q_full, QTILES * L::Q_BYTES);
 #pragma unroll
       for (int i = 0; i < QTILES; ++i)
 #pragma unroll
         for (int d = 0; d < D / 64; ++d)
           tma_load_3d(smem + L::Q_OFF + i * L::Q_BYTES + d * (BM * 128), &tq, &ctl->q_full, d * 64, q0 + i * BM, bh);
-      for (int j = 0; j < n_max && ok; ++j) {
-        const int s = j & 1;
-        const uint32_t ph = (j >> 1) & 1;
-        if (!mbar_wait_bounded(&ctl->kv_empty[s], ph ^ 1, p.wait_limit, abort_flag)) {
-          if (!*abort_flag) fa2_abort(ctl, NTL_STATUS_TMA_EMPTY_WAIT);
-          ok = false;
-          break;
-        }
-        const int k0 = j * BN;
+      // Issue order K0, K1, V0, K2, V1, ...: K runs one tile ahead of V.
+      int k_issued = 0, v_issued = 0;
+      auto load_k = [&](int j) -> bool {
+        const int s = j % KSTAGES;
+        if (!mbar_wait_bounded(&ctl->k_empty[s], ((j / KSTAGES) & 1) ^ 1, p.wait_limit, abort_flag)) return false;
         mbar_arrive_expect_tx(&ctl->k_full[s], L::KV_BYTES);
 #pragma unroll
         for (int d = 0; d < D / 64; ++d)
-          tma_load_3d(smem + L::K_OFF + s * L::KV_BYTES + d * (BN * 128), &tk, &ctl->k_full[s], d * 64, k0, bh);
+          tma_load_3d(smem + L::K_OFF + s * L::KV_BYTES + d * (BN * 128), &tk, &ctl->k_full[s], d * 64, j * BN, bh);
+        ++k_issued;
+        return true;
+      };
+      auto load_v = [&](int j) -> bool {
+        const int s = j % VSTAGES;
+        if (!mbar_wait_bounded(&ctl->v_empty[s], ((j / VSTAGES) & 1) ^ 1, p.wait_limit, abort_flag)) return false;
         mbar_arrive_expect_tx(&ctl->v_full[s], L::KV_BYTES);
 #pragma unroll
         for (int d = 0; d < D / 64; ++d)
-          tma_load_3d(smem + L::V_OFF + s * L::KV_BYTES + d * (BN * 128), &tv, &ctl->v_full[s], d * 64, k0, bh);
-        ++issued;
+          tma_load_3d(smem + L::V_OFF + s * L::KV_BYTES + d * (BN * 128), &tv, &ctl->v_full[s], d * 64, j * BN, bh);
+        ++v_issued;
+        return true;
+      };
+      if (n_max > 0) ok = load_k(0);
+      for (int j = 0; j < n_max && ok; ++j) {
+        if (j + 1 < n_max && !load_k(j + 1)) ok = false;
+        else if (!load_v(j)) ok = false;
       }
+      if (!ok && !*abort_flag) fa2_abort(ctl, NTL_STATUS_TMA_EMPTY_WAIT);
       if (!ok) {
         // Drain every copy this thread issued before the CTA exits.
         if (!mbar_wait_bounded(&ctl->q_full, 0, int64_t(1) << 24, nullptr))
           atomicCAS(&g_fa2_status, 0u, NTL_STATUS_DRAIN_WAIT);
-        for (int j = max(0, issued - 2); j < issued; ++j) {
-          const int s = j & 1;
-          const uint32_t ph = (j >> 1) & 1;
-          if (!mbar_wait_bounded(&ctl->k_full[s], ph, int64_t(1) << 24, nullptr) ||
-              !mbar_wait_bounded(&ctl->v_full[s], ph, int64_t(1) << 24, nullptr))
+        for (int j = max(0, k_issued - KSTAGES); j < k_issued; ++j)
+          if (!mbar_wait_bounded(&ctl->k_full[j % KSTAGES], (j / KSTAGES) & 1, int64_t(1) << 24, nullptr))
             atomicCAS(&g_fa2_status, 0u, NTL_STATUS_DRAIN_WAIT);
-        }
+        for (int j = max(0, v_issued - VSTAGES); j < v_issued; ++j)
+          if (!mbar_wait_bounded(&ctl->v_full[j % VSTAGES], (j / VSTAGES) & 1, int64_t(1) << 24, nullptr))
+            atomicCAS(&g_fa2_status, 0u, NTL_STATUS_DRAIN_WAIT);
       }
     }
   } else if (warp == MMA_WARP) {
@@ -217,7 +241,7 @@ __global__ void __launch_bounds__(THREADS, 1) fa2_fwd_kernel(const __grid_consta
       };
       auto issue_s = [&](int i, int j) {  // S_i = Q_i K_j^T
         const uint32_t q_addr = smem_u32(smem + L::Q_OFF + i * L::Q_BYTES);
-        const uint32_t k_addr = smem_u32(smem + L::K_OFF + (j & 1) * L::KV_BYTES);
+        const uint32_t k_addr = smem_u32(smem + L::K_OFF + (j % KSTAGES) * L::KV_BYTES);
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
           const uint32_t off = (kk >> 2) * (BM * 128) + (kk & 3) * 32;
@@ -230,26 +254,27 @@ __global__ void __launch_bounds__(THREADS, 1) fa2_fwd_kernel(const __grid_consta
         tc_fence_after();
         for (int i = 0; i < QTILES; ++i)
           if (n_t[i] > 0) issue_s(i, 0);
+        tc_commit(&ctl->k_empty[0]);  // K_0 is free once both QK^T retire
       } else {
         ok = false;
       }
       for (int j = 0; j < n_max && ok; ++j) {
-        const int s = j & 1;
+        const int s = j % VSTAGES;
         for (int i = 0; i < QTILES && ok; ++i) {
           if (j >= n_t[i]) continue;
-          if (!wait_or_abort(&ctl->sm_done[i], j & 1) || !wait_or_abort(&ctl->v_full[s], (j >> 1) & 1)) {
+          if (!wait_or_abort(&ctl->sm_done[i], j & 1) || !wait_or_abort(&ctl->v_full[s], (j / VSTAGES) & 1)) {
             ok = false;
             break;
           }
           tc_fence_after();
           const uint32_t v_addr = smem_u32(smem + L::V_OFF + s * L::KV_BYTES);
 #pragma unroll
-          for (int kk = 0; kk < BN / 16; ++kk)  // P_i: 8 packed columns per 16 keys
-            tc_mma_f16_ts(tmem + L::O_COL(i), tmem + L::S_COL(i) + kk * 8,
+          for (int kk = 0; kk < BN / 16; ++kk)  // P_i: keys [64h, 64h+64) packed at S columns [64h, 64h+32)
+            tc_mma_f16_ts(tmem + L::O_COL(i), tmem + L::S_COL(i) + (kk >> 2) * 64 + (kk & 3) * 8,
                           umma_desc_sw128(v_addr + kk * 2048, BN * 128, 1024), idesc_o, (j > 0 || kk > 0) ? 1u : 0u);
           if (j == n_t[i] - 1) tc_commit(&ctl->o_final[i]);
           if (j + 1 < n_t[i]) {
-            if (!wait_or_abort(&ctl->k_full[(j + 1) & 1], ((j + 1) >> 1) & 1)) {
+            if (!wait_or_abort(&ctl->k_full[(j + 1) % KSTAGES], ((j + 1) / KSTAGES) & 1)) {
               ok = false;
               break;
             }
@@ -257,7 +282,10 @@ __global__ void __launch_bounds__(THREADS, 1) fa2_fwd_kernel(const __grid_consta
             issue_s(i, j + 1);
           }
         }
-        if (ok) tc_commit(&ctl->kv_empty[s]);
+        if (ok) {
+          tc_commit(&ctl->v_empty[s]);                                    // V_j consumed by both P V
+          if (j + 1 < n_max) tc_commit(&ctl->k_empty[(j + 1) % KSTAGES]);  // K_{j+1} by both QK^T
+        }
       }
       if (!ok) {
         tc_commit(&ctl->drain);
@@ -265,22 +293,26 @@ __global__ void __launch_bounds__(THREADS, 1) fa2_fwd_kernel(const __grid_consta
           atomicCAS(&g_fa2_status, 0u, NTL_STATUS_DRAIN_WAIT);
       }
     }
-  } else if (warp < 8) {
+  } else if (warp < 2 * SM_WARPS_PER_TILE) {
     // ------------------------------------------------------------------ softmax warps
-    const int i = warp >> 2;  // query tile
+    // Warp w: query tile w/8, key half h = (w/4)&1 (keys [64h, 64h+64) of every KV tile and
+    // O columns [h*D/2, (h+1)*D/2)), TMEM lanes 32*(w&3)...: two threads per row.
+    const int i = warp >> 3;
+    const int h = (warp >> 2) & 1;
     const int quarter = warp & 3;
     const int r = quarter * 32 + lane;
     const int tile_q0 = q0 + i * BM;
     const int qrow = tile_q0 + r;
     const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
-    const uint32_t s_addr = tmem + lane_off + L::S_COL(i);
-    const uint32_t o_addr = tmem + lane_off + L::O_COL(i);
+    const uint32_t s_addr = tmem + lane_off + L::S_COL(i) + h * 64;  // this half's 64 S columns
+    const uint32_t o_addr = tmem + lane_off + L::O_COL(i) + h * (D / 2);
+    uint64_t* pair_bar = &ctl->pair[i][quarter];  // exchange barrier with the other half's warp
     const float c = p.c;
     const int key_lim = p.causal ? min(p.S, qrow + 1) : p.S;  // keys < key_lim are kept
-    float m_use = -INFINITY, l = 0.0f;
+    float m_use = -INFINITY, l = 0.0f;  // l: this half's share of the row sum
     bool ok = true;
     for (int j = 0; j < n_t[i]; ++j) {
-      const int k0 = j * BN;
+      const int k0 = j * BN + h * 64;  // first key of this half
       if (!mbar_wait_bounded(&ctl->s_full[i], j & 1, p.wait_limit, abort_flag)) {
         if (!*abort_flag) fa2_abort(ctl, NTL_STATUS_SOFTMAX_WAIT);
         ok = false;
@@ -288,37 +320,50 @@ __global__ void __launch_bounds__(THREADS, 1) fa2_fwd_kernel(const __grid_consta
       }
       __syncwarp();
       tc_fence_after();
-      const bool masked_tile = (k0 + BN > p.S) || (p.causal && k0 + BN - 1 > tile_q0);
-      uint32_t v[BN];
+      const bool masked_tile = (j * BN + BN > p.S) || (p.causal && j * BN + BN - 1 > tile_q0);
+      // pass 1: max over this half, combined with the other half through shared memory
+      float hmax;
+      {
+        uint32_t a[32], b[32];
+        tmem_ld_32x32b_x32(s_addr, a);
+        tmem_ld_32x32b_x32(s_addr + 32, b);
+        tc_wait_ld();
+        float cm[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+        if (masked_tile) {
 #pragma unroll
-      for (int ch = 0; ch < BN / 32; ++ch) tmem_ld_32x32b_x32(s_addr + ch * 32, *reinterpret_cast<uint32_t(*)[32]>(v + ch * 32));
-      tc_wait_ld();
-      if (masked_tile) {
+          for (int e = 0; e < 32; ++e) {
+            cm[e & 3] = fmaxf(cm[e & 3], k0 + e < key_lim ? __uint_as_float(a[e]) : -INFINITY);
+            cm[e & 3] = fmaxf(cm[e & 3], k0 + 32 + e < key_lim ? __uint_as_float(b[e]) : -INFINITY);
+          }
+        } else {
 #pragma unroll
-        for (int e = 0; e < BN; ++e)
-          if (k0 + e >= key_lim) v[e] = __float_as_uint(-INFINITY);
+          for (int e = 0; e < 32; ++e) cm[e & 3] = fmax3(cm[e & 3], __uint_as_float(a[e]), __uint_as_float(b[e]));
+        }
+        hmax = fmax3(fmaxf(cm[0], cm[1]), cm[2], cm[3]);
       }
-      // Row max with 8 independent partial maxima (a short dependency chain).
-      float pm[8];
-#pragma unroll
-      for (int a = 0; a < 8; ++a) pm[a] = __uint_as_float(v[a]);
-#pragma unroll
-      for (int e = 8; e < BN; ++e) pm[e & 7] = fmaxf(pm[e & 7], __uint_as_float(v[e]));
-      const float mx = fmaxf(fmaxf(fmaxf(pm[0], pm[1]), fmaxf(pm[2], pm[3])), fmaxf(fmaxf(pm[4], pm[5]), fmaxf(pm[6], pm[7])));
-      const float m_new = fmaxf(m_use, mx);
+      ctl->xmax[i][h][r] = hmax;
+      __syncwarp();
+      if (lane == 0) mbar_arrive(pair_bar);
+      if (!mbar_wait_bounded(pair_bar, j & 1, p.wait_limit, abort_flag)) {
+        if (!*abort_flag) fa2_abort(ctl, NTL_STATUS_SOFTMAX_WAIT);
+        ok = false;
+        break;
+      }
+      const float mx = fmaxf(hmax, ctl->xmax[i][h ^ 1][r]);
+      // lazy max (both halves take the same decision from the same values)
       float rs = 1.0f;
-      bool rescale = false;
+      bool moved = false;
       if (j == 0) {
-        m_use = m_new;
-      } else if ((m_new - m_use) * c > kRescaleLog2) {
-        rs = ex2_approx((m_use - m_new) * c);
-        m_use = m_new;
-        rescale = true;
+        m_use = mx;
+      } else if ((mx - m_use) * c > kRescaleLog2) {
+        rs = ex2_approx((m_use - mx) * c);
+        m_use = mx;
+        moved = true;
       }
-      if (__any_sync(0xffffffffu, rescale)) {
+      if (__any_sync(0xffffffffu, moved)) {
         // O_i = P_{<j} V is complete: S_i of this tile was issued after the last P_i V.
 #pragma unroll 1
-        for (int ch = 0; ch < D / 16; ++ch) {
+        for (int ch = 0; ch < D / 32; ++ch) {
           uint32_t o[16];
           tmem_ld_32x32b_x16(o_addr + ch * 16, o);
           tc_wait_ld();
@@ -327,54 +372,78 @@ __global__ void __launch_bounds__(THREADS, 1) fa2_fwd_kernel(const __grid_consta
           tmem_st_32x32b_x16(o_addr + ch * 16, o);
         }
       }
+      // pass 2: p = exp2(s*c - m*c) -> fp16 P packed over this half's own S columns
       const float mc = m_use * c;
-      float ps[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};  // independent partial sums
+      const uint64_t c2 = f2_make(c, c), nmc2 = f2_make(-mc, -mc);
+      uint64_t acc2[4] = {0ull, 0ull, 0ull, 0ull};
+#pragma unroll 1
+      for (int ch = 0; ch < 2; ++ch) {
+        uint32_t v[32];
+        tmem_ld_32x32b_x32(s_addr + ch * 32, v);
+        tc_wait_ld();
+        if (masked_tile) {
 #pragma unroll
-      for (int ch = 0; ch < BN / 32; ++ch) {
+          for (int e = 0; e < 32; ++e)
+            if (k0 + ch * 32 + e >= key_lim) v[e] = __float_as_uint(-INFINITY);
+        }
         uint32_t pk[16];
 #pragma unroll
         for (int e = 0; e < 16; ++e) {
-          // masked scores are -inf: exp2 gives exactly 0
-          const float x0 = __fmaf_rn(__uint_as_float(v[ch * 32 + 2 * e]), c, -mc);
-          const float x1 = __fmaf_rn(__uint_as_float(v[ch * 32 + 2 * e + 1]), c, -mc);
-          const bool on_fma = (e & 3) == 3;  // a fixed quarter of the pairs
-          const float p0 = on_fma ? exp2_fma(x0) : ex2_approx(x0);
-          const float p1 = on_fma ? exp2_fma(x1) : ex2_approx(x1);
-          ps[e & 7] += p0 + p1;
+          const uint64_t x2 = f2_fma(f2_make(__uint_as_float(v[2 * e]), __uint_as_float(v[2 * e + 1])), c2, nmc2);
+          float p0, p1;
+          if ((e & 3) == 3) {  // a fixed quarter of the pairs on the FMA pipe
+            exp2_fma2(x2, p0, p1);
+          } else {
+            float x0, x1;
+            f2_split(x2, x0, x1);
+            p0 = ex2_approx(x0);
+            p1 = ex2_approx(x1);
+          }
+          acc2[e & 3] = f2_add(acc2[e & 3], f2_make(p0, p1));
           pk[e] = pack_half2(p0, p1);
         }
-        // P keys [32*ch, 32*ch + 32) -> packed columns [16*ch, 16*ch + 16) of S_i (S is in registers).
+        // keys [k0 + 32ch, +32) -> packed columns [16ch, 16ch + 16) of this half (already read)
         tmem_st_32x32b_x16(s_addr + ch * 16, pk);
       }
-      const float sum = ((ps[0] + ps[1]) + (ps[2] + ps[3])) + ((ps[4] + ps[5]) + (ps[6] + ps[7]));
+      float sum;
+      {
+        float a0, a1;
+        f2_split(f2_add(f2_add(acc2[0], acc2[1]), f2_add(acc2[2], acc2[3])), a0, a1);
+        sum = a0 + a1;
+      }
       l = (j == 0) ? sum : __fmaf_rn(l, rs, sum);
       tc_wait_st();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&ctl->sm_done[i]);
     }
-    // epilogue: O / l -> fp16
+    // epilogue: O / (l_0 + l_1) -> fp16, each half its D/2 columns
     if (ok && n_t[i] > 0) {
-      if (!mbar_wait_bounded(&ctl->o_final[i], 0, p.wait_limit, abort_flag)) {
+      ctl->xmax[i][h][r] = l;
+      __syncwarp();
+      if (lane == 0) mbar_arrive(pair_bar);
+      const bool paired = mbar_wait_bounded(pair_bar, n_t[i] & 1, p.wait_limit, abort_flag);
+      const float l_row = l + ctl->xmax[i][h ^ 1][r];
+      if (!paired || !mbar_wait_bounded(&ctl->o_final[i], 0, p.wait_limit, abort_flag)) {
         if (!*abort_flag) fa2_abort(ctl, NTL_STATUS_SOFTMAX_WAIT);
       } else {
         __syncwarp();
         tc_fence_after();
-        const float inv_l = 1.0f / l;
-        __half* orow = p.o + (static_cast<int64_t>(bh) * p.S + qrow) * D;
+        const float inv_l = 1.0f / l_row;
+        __half* orow = p.o + (static_cast<int64_t>(bh) * p.S + qrow) * D + h * (D / 2);
 #pragma unroll 1
-        for (int ch = 0; ch < D / 16; ++ch) {
+        for (int ch = 0; ch < D / 32; ++ch) {
           uint32_t o[16];
           tmem_ld_32x32b_x16(o_addr + ch * 16, o);
           tc_wait_ld();
           if (qrow < p.S) {
-            uint32_t h[8];
+            uint32_t hv[8];
 #pragma unroll
             for (int e = 0; e < 8; ++e)
-              h[e] = pack_half2(__uint_as_float(o[2 * e]) * inv_l, __uint_as_float(o[2 * e + 1]) * inv_l);
+              hv[e] = pack_half2(__uint_as_float(o[2 * e]) * inv_l, __uint_as_float(o[2 * e + 1]) * inv_l);
             uint4* dst = reinterpret_cast<uint4*>(orow + ch * 16);
-            dst[0] = make_uint4(h[0], h[1], h[2], h[3]);
-            dst[1] = make_uint4(h[4], h[5], h[6], h[7]);
+            dst[0] = make_uint4(hv[0], hv[1], hv[2], hv[3]);
+            dst[1] = make_uint4(hv[4], hv[5], hv[6], hv[7]);
           }
         }
       }
