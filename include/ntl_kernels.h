@@ -88,6 +88,21 @@ enum { NTL_BIAS_NONE = 0, NTL_BIAS_N = 1, NTL_BIAS_MN = 2, NTL_BIAS_M = 3 };
 int ntl_gemm_f16_f32(const uint16_t* a, const uint16_t* b, float* c, const float* bias, int bias_mode,
                      float alpha, int relu, int64_t M, int64_t N, int64_t K, int b_trans, ntl_stream_t stream);
 
+/* Workspace (bytes) ntl_gemm_f16_f32_ws needs for this shape on the current device; 0 when
+ * every output tile is computed data-parallel.  Same reference counterpart as
+ * ntl_gemm_f16_f32 (the workspace replaces nothing in the reference: its GEMM has no
+ * cross-CTA reduction). */
+int ntl_gemm_workspace_size(int64_t M, int64_t N, int64_t K, int b_trans, uint64_t* bytes_out);
+
+/* ntl_gemm_f16_f32 with a caller-owned workspace of at least ntl_gemm_workspace_size bytes
+ * (16-byte aligned, zero-filled before its first use; every successful call leaves its flag
+ * words zero again).  The last, partial wave of output tiles is split along K over all SMs
+ * (stream-K) and reduced through the workspace.  Calls sharing a workspace must not overlap
+ * on the GPU.  Replaces the same FFI call as ntl_gemm_f16_f32 (codegen.py:969-1026). */
+int ntl_gemm_f16_f32_ws(const uint16_t* a, const uint16_t* b, float* c, const float* bias, int bias_mode,
+                        float alpha, int relu, int64_t M, int64_t N, int64_t K, int b_trans, void* workspace,
+                        uint64_t workspace_bytes, ntl_stream_t stream);
+
 /* FlashAttention-2 forward, fp16 Q,K,V,O [batch, heads, seq, dim] row-major.
  *   O = softmax_base2((Q K^T) * scale_log2 [causal: key <= query]) V, with P rounded to fp16
  *   before the P V product and fp32 softmax statistics.

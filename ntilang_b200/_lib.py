@@ -31,6 +31,10 @@ SIGNATURES = {
     "ntl_gemm_f16_f32": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, c_f32p, c_f32p, ctypes.c_int,
                                         ctypes.c_float, ctypes.c_int, c_i64, c_i64, c_i64, ctypes.c_int,
                                         ctypes.c_void_p]),
+    "ntl_gemm_workspace_size": (ctypes.c_int, [c_i64, c_i64, c_i64, ctypes.c_int, ctypes.POINTER(ctypes.c_uint64)]),
+    "ntl_gemm_f16_f32_ws": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, c_f32p, c_f32p, ctypes.c_int,
+                                           ctypes.c_float, ctypes.c_int, c_i64, c_i64, c_i64, ctypes.c_int,
+                                           ctypes.c_void_p, ctypes.c_uint64, ctypes.c_void_p]),
     "ntl_fa2_fwd_f16": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, c_i64,
                                        c_i64, c_i64, c_i64, ctypes.c_float, ctypes.c_int, ctypes.c_void_p]),
     "ntl_device_status": (ctypes.c_int, [ctypes.POINTER(ctypes.c_uint32)]),
@@ -95,9 +99,16 @@ def set_wait_limit(polls: int) -> None:
     call("ntl_set_wait_limit", int(polls))
 
 
+def gemm_workspace_size(M, N, K, b_trans) -> int:
+    out = ctypes.c_uint64(0)
+    call("ntl_gemm_workspace_size", int(M), int(N), int(K), int(b_trans), ctypes.byref(out))
+    return int(out.value)
+
+
 def launch_count() -> int:
     return int(lib().ntl_launch_count())
 
 
-__all__ = ["KernelError", "SIGNATURES", "call", "clear_device_status", "device_status", "launch_count", "lib",
+__all__ = ["KernelError", "SIGNATURES", "call", "clear_device_status", "device_status", "gemm_workspace_size",
+           "launch_count", "lib",
            "library_path", "set_wait_limit"]

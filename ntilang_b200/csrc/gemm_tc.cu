@@ -13,10 +13,17 @@
 //   warps 2..5  epilogue: tcgen05.ld 32 lanes x 32 columns, alpha / bias / ReLU in registers,
 //               128-bit stores to C.  The double-buffered accumulator lets the epilogue of
 //               tile i overlap the main loop of tile i+1.
-// Every mbarrier wait is bounded (ntl_set_wait_limit); a wait that gives up records a
-// status code, raises the CTA abort flag, drains in-flight TMA loads and MMAs, frees TMEM
-// and returns.  Shapes TMA cannot address (K or N not a multiple of 8, unaligned pointers)
-// use a CUDA-core tiled kernel with the same epilogue.
+// Work schedule: whole waves of output tiles are data-parallel (one CTA computes a tile over
+// all of K).  With a workspace (ntl_gemm_f16_f32_ws), the tiles of the last, partial wave
+// are split along K evenly over all CTAs (stream-K): a CTA that starts a tile mid-K writes
+// its fp32 partial sum to its workspace slot and raises its flag; the CTA holding the
+// tile's first k-block waits for those flags (bounded), adds the partials and runs the
+// epilogue.  Without a workspace every tile is data-parallel.
+// Every mbarrier / flag wait is bounded (ntl_set_wait_limit and a 2 s wall-clock cap); a
+// wait that gives up records a status code, raises the CTA abort flag, drains in-flight TMA
+// loads and MMAs, frees TMEM and returns.  Shapes TMA cannot address (K or N not a
+// multiple of 8, unaligned pointers) use a CUDA-core tiled kernel with the same epilogue.
+#include <algorithm>
 #include <atomic>
 #include <mutex>
 
@@ -32,6 +39,8 @@ constexpr int THREADS = 192;
 constexpr int TMEM_COLS = 512;
 constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*barriers*/ + 1024 /*alignment slack*/;
 constexpr int GROUP_M = 8;
+constexpr int SK_MIN_UNITS = 8;             // fewest k-blocks a stream-K CTA takes
+constexpr size_t SK_SLOT_FLOATS = size_t(BM) * BN;
 
 __device__ uint32_t g_gemm_status;
 
@@ -45,6 +54,13 @@ struct GemmParams {
   int b_trans;
   int vec_store;  // C rows 16-byte aligned
   int64_t wait_limit;
+  // work plan
+  int num_m, num_n, kb;  // tile grid and k-blocks per tile
+  int dp_tiles;          // tiles [0, dp_tiles) are data-parallel
+  int sk_ctas;           // CTAs [0, sk_ctas) share the k-blocks of tiles [dp_tiles, tiles)
+  int64_t sk_units;
+  float* ws;             // sk_ctas partial-sum slots of BM x BN fp32
+  uint32_t* flags;       // sk_ctas flags (0 = empty, 1 = partial ready)
 };
 
 struct __align__(8) SharedCtl {
@@ -53,8 +69,48 @@ struct __align__(8) SharedCtl {
   uint64_t acc_full[2];
   uint64_t acc_empty[2];
   uint64_t drain;
+  uint64_t sk_stored;  // epilogue warps finished writing a partial
+  uint64_t sk_read;    // epilogue warps saw every contributor flag of a finalised tile
   uint32_t tmem_base;
   int abort;
+};
+
+struct Work {
+  int tile;
+  int k0, k1;  // k-block range [k0, k1)
+};
+
+// The ordered list of work items of one CTA: its data-parallel tiles, then its stream-K
+// segments.  Every role walks the same list.
+struct WorkIter {
+  int t;
+  int64_t u, u_end;
+  __device__ __forceinline__ static int64_t sk_begin(const GemmParams& p, int cta) {
+    return cta >= p.sk_ctas ? p.sk_units : (p.sk_units * cta) / p.sk_ctas;
+  }
+  __device__ __forceinline__ void init(const GemmParams& p) {
+    t = blockIdx.x;
+    u = sk_begin(p, blockIdx.x);
+    u_end = sk_begin(p, blockIdx.x + 1);
+    if (static_cast<int>(blockIdx.x) >= p.sk_ctas) u = u_end = 0;
+  }
+  __device__ __forceinline__ bool next(const GemmParams& p, Work& w) {
+    if (t < p.dp_tiles) {
+      w.tile = t, w.k0 = 0, w.k1 = p.kb;
+      t += gridDim.x;
+      return true;
+    }
+    if (u < u_end) {
+      const int64_t local = u / p.kb;
+      w.tile = p.dp_tiles + static_cast<int>(local);
+      w.k0 = static_cast<int>(u - local * p.kb);
+      const int64_t rest = u_end - u;
+      w.k1 = rest < static_cast<int64_t>(p.kb - w.k0) ? w.k0 + static_cast<int>(rest) : p.kb;
+      u += w.k1 - w.k0;
+      return true;
+    }
+    return false;
+  }
 };
 
 __device__ __forceinline__ void tile_coords(int t, int num_m, int num_n, int& mb, int& nb) {
@@ -79,6 +135,26 @@ __device__ __forceinline__ float epi(float acc, float alpha, float b, int relu, 
   return relu ? fmaxf(v, 0.0f) : v;
 }
 
+__device__ __forceinline__ uint32_t ld_acquire_u32(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Bounded wait for a stream-K contributor flag (2 s wall-clock cap, abort-aware).
+__device__ __forceinline__ bool wait_flag(const uint32_t* flag, int64_t limit, volatile int* abort_flag) {
+  const uint64_t t0 = global_ns();
+  for (int64_t i = 0; i < limit; ++i) {
+    if (ld_acquire_u32(flag) != 0u) return true;
+    if ((i & 63) == 63) {
+      if (*abort_flag) return false;
+      if (global_ns() - t0 > kWaitCapNs) return false;
+      __nanosleep(64);
+    }
+  }
+  return false;
+}
+
 __global__ void __launch_bounds__(THREADS, 1) gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_a,
                                                              const __grid_constant__ CUtensorMap tmap_b,
                                                              const GemmParams p) {
@@ -91,10 +167,6 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_tc_kernel(const __grid_consta
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int num_m = (p.M + BM - 1) / BM;
-  const int num_n = (p.N + BN - 1) / BN;
-  const int num_tiles = num_m * num_n;
-  const int num_kb = (p.K + BK - 1) / BK;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -106,6 +178,8 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_tc_kernel(const __grid_consta
       mbar_init(&ctl->acc_empty[a], 4);  // one arrival per epilogue warp
     }
     mbar_init(&ctl->drain, 1);
+    mbar_init(&ctl->sk_stored, 4);
+    mbar_init(&ctl->sk_read, 4);
     ctl->abort = 0;
     fence_mbar_init();
     prefetch_tensormap(&tmap_a);
@@ -127,11 +201,14 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_tc_kernel(const __grid_consta
       uint32_t phase = 0;
       int issued = 0;
       bool ok = true;
-      for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
+      WorkIter it;
+      it.init(p);
+      Work w;
+      while (ok && it.next(p, w)) {
         int mb, nb;
-        tile_coords(t, num_m, num_n, mb, nb);
+        tile_coords(w.tile, p.num_m, p.num_n, mb, nb);
         const int m0 = mb * BM, n0 = nb * BN;
-        for (int kb = 0; kb < num_kb; ++kb) {
+        for (int kb = w.k0; kb < w.k1; ++kb) {
           if (!mbar_wait_bounded(&ctl->empty[stage], phase ^ 1, p.wait_limit, abort_flag)) {
             if (!*abort_flag) record_abort(ctl, NTL_STATUS_TMA_EMPTY_WAIT);
             ok = false;
@@ -171,7 +248,10 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_tc_kernel(const __grid_consta
       uint32_t phase = 0;
       int local = 0;
       bool ok = true;
-      for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x, ++local) {
+      WorkIter it;
+      it.init(p);
+      Work w;
+      for (; ok && it.next(p, w); ++local) {
         const int acc = local & 1;
         const uint32_t acc_phase = (local >> 1) & 1;
         if (!mbar_wait_bounded(&ctl->acc_empty[acc], acc_phase ^ 1, p.wait_limit, abort_flag)) {
@@ -181,7 +261,7 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_tc_kernel(const __grid_consta
         }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * BN;
-        for (int kb = 0; kb < num_kb; ++kb) {
+        for (int kb = w.k0; kb < w.k1; ++kb) {
           if (!mbar_wait_bounded(&ctl->full[stage], phase, p.wait_limit, abort_flag)) {
             if (!*abort_flag) record_abort(ctl, NTL_STATUS_MMA_FULL_WAIT);
             ok = false;
@@ -195,7 +275,7 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_tc_kernel(const __grid_consta
             const uint64_t adesc = umma_desc_sw128(a_addr + k * 32, 16, 1024);
             const uint64_t bdesc = p.b_trans ? umma_desc_sw128(b_addr + k * 32, 16, 1024)
                                              : umma_desc_sw128(b_addr + k * 2048, 64 * BK * 2, 1024);
-            tc_mma_f16_ss(d_tmem, adesc, bdesc, idesc, (kb > 0 || k > 0) ? 1u : 0u);
+            tc_mma_f16_ss(d_tmem, adesc, bdesc, idesc, (kb > w.k0 || k > 0) ? 1u : 0u);
           }
           tc_commit(&ctl->empty[stage]);
           if (++stage == STAGES) stage = 0, phase ^= 1;
@@ -213,10 +293,15 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_tc_kernel(const __grid_consta
   } else {
     // ------------------------------------------------------------ epilogue (warps 2..5)
     const int quarter = warp & 3;  // TMEM lanes 32*quarter .. +31 are accessible to this warp
+    const int r_local = quarter * 32 + lane;
     int local = 0;
-    for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++local) {
+    int finalised = 0;  // stream-K tiles finalised so far (phase of sk_read)
+    WorkIter it;
+    it.init(p);
+    Work w;
+    for (; it.next(p, w); ++local) {
       int mb, nb;
-      tile_coords(t, num_m, num_n, mb, nb);
+      tile_coords(w.tile, p.num_m, p.num_n, mb, nb);
       const int acc = local & 1;
       const uint32_t acc_phase = (local >> 1) & 1;
       if (!mbar_wait_bounded(&ctl->acc_full[acc], acc_phase, p.wait_limit, abort_flag)) {
@@ -225,24 +310,83 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_tc_kernel(const __grid_consta
       }
       __syncwarp();
       tc_fence_after();
-      const int row = mb * BM + quarter * 32 + lane;
+      const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + acc * BN;
+      if (w.k0 > 0) {
+        // Stream-K contributor: raw partial sums -> this CTA's workspace slot, then its flag.
+        float* slot = p.ws + static_cast<size_t>(blockIdx.x) * SK_SLOT_FLOATS + static_cast<size_t>(r_local) * BN;
+        for (int chunk = 0; chunk < BN / 32; ++chunk) {
+          uint32_t r[32];
+          tmem_ld_32x32b_x32(t_row + chunk * 32, r);
+          tc_wait_ld();
+#pragma unroll
+          for (int j = 0; j < 32; j += 4)
+            __stcg(reinterpret_cast<float4*>(slot + chunk * 32 + j),
+                   make_float4(__uint_as_float(r[j]), __uint_as_float(r[j + 1]), __uint_as_float(r[j + 2]),
+                               __uint_as_float(r[j + 3])));
+        }
+        __threadfence();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&ctl->acc_empty[acc]);
+        if (lane == 0) mbar_arrive(&ctl->sk_stored);
+        if (warp == 2 && lane == 0) {
+          if (mbar_wait_bounded(&ctl->sk_stored, 0, p.wait_limit, abort_flag)) {
+            __threadfence();
+            atomicExch(p.flags + blockIdx.x, 1u);
+          } else if (!*abort_flag) {
+            record_abort(ctl, NTL_STATUS_ACC_FULL_WAIT);
+          }
+        }
+        continue;
+      }
+      // Contributors of this tile (stream-K finaliser): CTAs after this one whose range starts
+      // inside the tile.
+      int first_c = 0, last_c = -1;
+      if (w.k1 < p.kb) {
+        const int64_t tile_end_u = static_cast<int64_t>(w.tile - p.dp_tiles + 1) * p.kb;
+        first_c = blockIdx.x + 1;
+        last_c = blockIdx.x;
+        while (last_c + 1 < p.sk_ctas && WorkIter::sk_begin(p, last_c + 1) < tile_end_u) ++last_c;
+        bool ready = true;
+        for (int cc = first_c; cc <= last_c && ready; ++cc) {
+          if (lane == 0) ready = wait_flag(p.flags + cc, p.wait_limit, abort_flag);
+          ready = __shfl_sync(0xffffffffu, ready ? 1 : 0, 0) != 0;
+        }
+        if (!ready) {
+          if (!*abort_flag) record_abort(ctl, NTL_STATUS_ACC_FULL_WAIT);
+          break;
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&ctl->sk_read);
+      }
+      const int row = mb * BM + r_local;
       const bool row_ok = row < p.M;
       float* crow = p.c + static_cast<int64_t>(row) * p.N;
       const float row_bias = (p.bias_mode == NTL_BIAS_M && row_ok) ? __ldg(p.bias + row) : 0.0f;
       for (int chunk = 0; chunk < BN / 32; ++chunk) {
         uint32_t r[32];
-        tmem_ld_32x32b_x32(tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + acc * BN + chunk * 32, r);
+        tmem_ld_32x32b_x32(t_row + chunk * 32, r);
         tc_wait_ld();
+        float v[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+        for (int cc = first_c; cc <= last_c; ++cc) {
+          const float* part = p.ws + static_cast<size_t>(cc) * SK_SLOT_FLOATS + static_cast<size_t>(r_local) * BN + chunk * 32;
+#pragma unroll
+          for (int j = 0; j < 32; j += 4) {
+            const float4 q = __ldcg(reinterpret_cast<const float4*>(part + j));
+            v[j] += q.x, v[j + 1] += q.y, v[j + 2] += q.z, v[j + 3] += q.w;
+          }
+        }
         const int col0 = nb * BN + chunk * 32;
         if (!row_ok || col0 >= p.N) continue;
-        float v[32];
 #pragma unroll
         for (int j = 0; j < 32; ++j) {
           float b = row_bias;
           const int col = col0 + j;
           if (p.bias_mode == NTL_BIAS_N) b = (col < p.N) ? __ldg(p.bias + col) : 0.0f;
           else if (p.bias_mode == NTL_BIAS_MN) b = (col < p.N) ? __ldg(p.bias + static_cast<int64_t>(row) * p.N + col) : 0.0f;
-          v[j] = epi(__uint_as_float(r[j]), p.alpha, b, p.relu, p.bias_mode);
+          v[j] = epi(v[j], p.alpha, b, p.relu, p.bias_mode);
         }
         if (p.vec_store && col0 + 32 <= p.N) {
 #pragma unroll
@@ -257,6 +401,17 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_tc_kernel(const __grid_consta
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&ctl->acc_empty[acc]);
+      if (last_c >= first_c) {
+        // Every epilogue warp has seen the flags: reset them for the next launch.
+        if (warp == 2 && lane == 0) {
+          if (mbar_wait_bounded(&ctl->sk_read, finalised & 1, p.wait_limit, abort_flag)) {
+            for (int cc = first_c; cc <= last_c; ++cc) atomicExch(p.flags + cc, 0u);
+          } else if (!*abort_flag) {
+            record_abort(ctl, NTL_STATUS_ACC_FULL_WAIT);
+          }
+        }
+        ++finalised;
+      }
     }
   }
 
@@ -369,21 +524,45 @@ int ensure_smem_attr() {
   return NTL_OK;
 }
 
-}  // namespace
+// Work plan for an M x N x K problem.  Stream-K applies only with a workspace.
+struct Plan {
+  int num_m, num_n, tiles, kb, grid, dp_tiles, sk_ctas;
+  int64_t sk_units;
+  size_t ws_bytes;
+};
 
-uint32_t ntl_gemm_status_read(int clear) {
-  uint32_t v = 0;
-  if (cudaMemcpyFromSymbol(&v, g_gemm_status, sizeof(v)) != cudaSuccess) return 0;
-  if (clear) {
-    uint32_t z = 0;
-    cudaMemcpyToSymbol(g_gemm_status, &z, sizeof(z));
+int make_plan(int64_t M, int64_t N, int64_t K, bool stream_k, Plan* pl) {
+  int sms = 0;
+  if (int rc = ntl_num_sms(&sms)) return rc;
+  pl->num_m = static_cast<int>((M + BM - 1) / BM);
+  pl->num_n = static_cast<int>((N + BN - 1) / BN);
+  const int64_t tiles = static_cast<int64_t>(pl->num_m) * pl->num_n;
+  NTL_REQUIRE(tiles < (int64_t(1) << 31), NTL_ERR_UNSUPPORTED, "gemm: too many tiles");
+  pl->tiles = static_cast<int>(tiles);
+  pl->kb = static_cast<int>((K + BK - 1) / BK);
+  pl->grid = static_cast<int>(tiles < sms ? tiles : sms);
+  pl->dp_tiles = pl->tiles;
+  pl->sk_ctas = 0;
+  pl->sk_units = 0;
+  pl->ws_bytes = 0;
+  if (stream_k && pl->tiles % sms != 0) {
+    const int dp = (pl->tiles / sms) * sms;
+    const int64_t units = static_cast<int64_t>(pl->tiles - dp) * pl->kb;
+    const int64_t ctas = std::min<int64_t>(sms, units / SK_MIN_UNITS);
+    if (ctas >= 2) {
+      pl->grid = sms;
+      pl->dp_tiles = dp;
+      pl->sk_units = units;
+      pl->sk_ctas = static_cast<int>(ctas);
+      pl->ws_bytes = static_cast<size_t>(ctas) * SK_SLOT_FLOATS * sizeof(float) + static_cast<size_t>(ctas) * 4;
+    }
   }
-  return v;
+  return NTL_OK;
 }
 
-extern "C" int ntl_gemm_f16_f32(const uint16_t* a, const uint16_t* b, float* c, const float* bias, int bias_mode,
-                                float alpha, int relu, int64_t M, int64_t N, int64_t K, int b_trans,
-                                ntl_stream_t stream) {
+int gemm_launch(const uint16_t* a, const uint16_t* b, float* c, const float* bias, int bias_mode, float alpha,
+                int relu, int64_t M, int64_t N, int64_t K, int b_trans, void* ws, size_t ws_bytes, bool stream_k,
+                cudaStream_t s) {
   NTL_REQUIRE(M >= 0 && N >= 0 && K >= 0, NTL_ERR_INVALID, "gemm: negative size");
   NTL_REQUIRE(M < (int64_t(1) << 31) && N < (int64_t(1) << 31) && K < (int64_t(1) << 31), NTL_ERR_UNSUPPORTED,
               "gemm: dimensions must be < 2^31");
@@ -392,7 +571,6 @@ extern "C" int ntl_gemm_f16_f32(const uint16_t* a, const uint16_t* b, float* c, 
   NTL_REQUIRE(bias_mode == NTL_BIAS_NONE || bias != nullptr, NTL_ERR_INVALID, "gemm: bias_mode needs a bias pointer");
   if (M == 0 || N == 0) return NTL_OK;
   NTL_REQUIRE(c && (K == 0 || (a && b)), NTL_ERR_INVALID, "gemm: NULL pointer");
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
   GemmParams p;
   p.c = c;
   p.bias = bias;
@@ -411,6 +589,20 @@ extern "C" int ntl_gemm_f16_f32(const uint16_t* a, const uint16_t* b, float* c, 
     ntl_note_launch();
     return ntl_check_launch("gemm (CUDA-core path) launch");
   }
+  Plan pl;
+  if (int rc = make_plan(M, N, K, stream_k, &pl)) return rc;
+  if (pl.sk_ctas > 0) {
+    NTL_REQUIRE(ws != nullptr && ws_bytes >= pl.ws_bytes, NTL_ERR_INVALID,
+                "gemm: workspace of %zu bytes needed, %zu given", pl.ws_bytes, ws_bytes);
+    NTL_REQUIRE(ntl_aligned(ws, 16), NTL_ERR_ALIGNMENT, "gemm: workspace must be 16-byte aligned");
+  }
+  p.num_m = pl.num_m, p.num_n = pl.num_n, p.kb = pl.kb;
+  p.dp_tiles = pl.dp_tiles;
+  p.sk_ctas = pl.sk_ctas;
+  p.sk_units = pl.sk_units;
+  p.ws = static_cast<float*>(ws);
+  p.flags = pl.sk_ctas > 0 ? reinterpret_cast<uint32_t*>(static_cast<float*>(ws) + pl.sk_ctas * SK_SLOT_FLOATS)
+                           : nullptr;
   CUtensorMap ma, mb;
   if (int rc = make_map_f16(&ma, a, M, K, BK, BM)) return rc;
   if (b_trans) {
@@ -419,12 +611,44 @@ extern "C" int ntl_gemm_f16_f32(const uint16_t* a, const uint16_t* b, float* c, 
     if (int rc = make_map_f16(&mb, b, K, N, 64, BK)) return rc;
   }
   if (int rc = ensure_smem_attr()) return rc;
-  int sms = 0;
-  if (int rc = ntl_num_sms(&sms)) return rc;
-  const int64_t tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
-  NTL_REQUIRE(tiles < (int64_t(1) << 31), NTL_ERR_UNSUPPORTED, "gemm: too many tiles");
-  const int grid = static_cast<int>(tiles < sms ? tiles : sms);
-  gemm_tc_kernel<<<grid, THREADS, SMEM_BYTES, s>>>(ma, mb, p);
+  gemm_tc_kernel<<<pl.grid, THREADS, SMEM_BYTES, s>>>(ma, mb, p);
   ntl_note_launch();
   return ntl_check_launch("gemm (tcgen05 path) launch");
+}
+
+}  // namespace
+
+uint32_t ntl_gemm_status_read(int clear) {
+  uint32_t v = 0;
+  if (cudaMemcpyFromSymbol(&v, g_gemm_status, sizeof(v)) != cudaSuccess) return 0;
+  if (clear) {
+    uint32_t z = 0;
+    cudaMemcpyToSymbol(g_gemm_status, &z, sizeof(z));
+  }
+  return v;
+}
+
+extern "C" int ntl_gemm_f16_f32(const uint16_t* a, const uint16_t* b, float* c, const float* bias, int bias_mode,
+                                float alpha, int relu, int64_t M, int64_t N, int64_t K, int b_trans,
+                                ntl_stream_t stream) {
+  return gemm_launch(a, b, c, bias, bias_mode, alpha, relu, M, N, K, b_trans, nullptr, 0, false,
+                     static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int ntl_gemm_workspace_size(int64_t M, int64_t N, int64_t K, int b_trans, uint64_t* bytes_out) {
+  NTL_REQUIRE(bytes_out != nullptr, NTL_ERR_INVALID, "gemm_workspace_size: bytes_out is NULL");
+  NTL_REQUIRE(M >= 0 && N >= 0 && K >= 0, NTL_ERR_INVALID, "gemm_workspace_size: negative size");
+  *bytes_out = 0;
+  if (M == 0 || N == 0 || K == 0 || K % 8 != 0 || (!b_trans && N % 8 != 0)) return NTL_OK;
+  Plan pl;
+  if (int rc = make_plan(M, N, K, true, &pl)) return rc;
+  *bytes_out = pl.ws_bytes;
+  return NTL_OK;
+}
+
+extern "C" int ntl_gemm_f16_f32_ws(const uint16_t* a, const uint16_t* b, float* c, const float* bias, int bias_mode,
+                                   float alpha, int relu, int64_t M, int64_t N, int64_t K, int b_trans,
+                                   void* workspace, uint64_t workspace_bytes, ntl_stream_t stream) {
+  return gemm_launch(a, b, c, bias, bias_mode, alpha, relu, M, N, K, b_trans, workspace, workspace_bytes, true,
+                     static_cast<cudaStream_t>(stream));
 }

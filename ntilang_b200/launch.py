@@ -19,6 +19,25 @@ def _ptr(t):
     return t.data_ptr()
 
 
+_workspaces: dict = {}
+
+
+def gemm_workspace(device, nbytes: int):
+    """A zero-initialised workspace of at least ``nbytes`` on ``device``, cached per device.
+
+    The stream-K GEMM leaves its flag words zero after every successful call, so the buffer
+    is reused as is.  Calls that share it run in stream order on the caller's stream.
+    """
+    import torch
+
+    key = torch.device(device).index
+    buf = _workspaces.get(key)
+    if buf is None or buf.numel() < nbytes:
+        buf = torch.zeros(max(nbytes, 1 << 20), dtype=torch.uint8, device=device)
+        _workspaces[key] = buf
+    return buf
+
+
 def _size(value, tensor, dim):
     """Static size from the spec, or the bound value of a symbolic dimension."""
     return int(tensor.shape[dim]) if isinstance(value, str) else int(value)
@@ -49,8 +68,11 @@ def launch(spec: OpSpec, tensors, stream: int) -> None:
         bias = tensors[a["bias"]] if "bias" in a else None
         M, K = int(A.shape[0]), int(A.shape[1])
         N = int(B.shape[0]) if p["transpose_b"] else int(B.shape[1])
-        _lib.call("ntl_gemm_f16_f32", _ptr(A), _ptr(B), _ptr(C), _ptr(bias) if bias is not None else None,
-                  int(p["bias_mode"]), float(p["alpha"]), int(p["relu"]), M, N, K, int(p["transpose_b"]), stream)
+        nbytes = _lib.gemm_workspace_size(M, N, K, int(p["transpose_b"]))
+        ws = gemm_workspace(A.device, nbytes) if nbytes else None
+        _lib.call("ntl_gemm_f16_f32_ws", _ptr(A), _ptr(B), _ptr(C), _ptr(bias) if bias is not None else None,
+                  int(p["bias_mode"]), float(p["alpha"]), int(p["relu"]), M, N, K, int(p["transpose_b"]),
+                  _ptr(ws) if ws is not None else None, ws.numel() if ws is not None else 0, stream)
     elif f == "fa2":
         q, k, v, o = tensors[a["q"]], tensors[a["k"]], tensors[a["v"]], tensors[a["o"]]
         b, h, s, d = (int(x) for x in q.shape)
@@ -65,7 +87,7 @@ ABI_CALL = {
     "cumsum": "ntl_cumsum_f32(X, Y, rows, cols, reverse, stream)",
     "softmax": "ntl_softmax_f32(X, Y, rows, cols, stream)",
     "rmsnorm": "ntl_rmsnorm_f32(X, W, Y, rows, cols, eps, inv_n, stream)",
-    "gemm": "ntl_gemm_f16_f32(A, B, C, bias, bias_mode, alpha, relu, M, N, K, b_trans, stream)",
+    "gemm": "ntl_gemm_f16_f32_ws(A, B, C, bias, bias_mode, alpha, relu, M, N, K, b_trans, workspace, bytes, stream)",
     "fa2": "ntl_fa2_fwd_f16(Q, K, V, O, batch, heads, seq, dim, scale_log2, causal, stream)",
 }
 

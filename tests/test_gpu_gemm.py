@@ -145,3 +145,52 @@ def test_gemm_timeout_path_reports_error(torch_cuda):
     # the context still works
     c2 = K.matmul(512, 512, 512)(a, b)
     check(torch, c2, ref_gemm(torch, a, b))
+
+
+@pytest.mark.parametrize("m,n,k", [(4096, 4096, 4096), (512, 4096, 4096), (1000, 1024, 1032), (384, 768, 4096)])
+def test_gemm_stream_k_repeated_calls(torch_cuda, m, n, k):
+    """Shapes whose last wave is split along K (stream-K through the cached workspace), called
+    three times in a row: the contributor flags must be back to zero after every call."""
+    torch = torch_cuda
+    from ntilang_b200 import _lib
+
+    assert _lib.gemm_workspace_size(m, n, k, 0) > 0
+    gen = torch.Generator(device="cuda").manual_seed(m + k)
+    a = (torch.randn(m, k, device="cuda", generator=gen) / k**0.5).half()
+    b = torch.randn(k, n, device="cuda", generator=gen).half()
+    bias = torch.randn(n, device="cuda", generator=gen) * 0.1
+    kern = K.matmul_bias_relu(m, n, k)
+    ref = torch.relu(ref_gemm(torch, a, b) + bias)
+    for _ in range(3):
+        c = kern(a, b, bias)
+        check(torch, c, ref)
+
+
+def test_gemm_stream_k_matches_data_parallel_entry(torch_cuda):
+    torch = torch_cuda
+    from ntilang_b200 import _lib
+
+    m = n = k = 2048
+    a = torch.randn(m, k, device="cuda").half()
+    b = torch.randn(k, n, device="cuda").half()
+    c_dp = torch.empty(m, n, device="cuda")
+    s = torch.cuda.current_stream().cuda_stream
+    _lib.call("ntl_gemm_f16_f32", a.data_ptr(), b.data_ptr(), c_dp.data_ptr(), None, 0, 1.0, 0, m, n, k, 0, s)
+    c_sk = K.matmul(m, n, k)(a, b)
+    check(torch, c_sk, c_dp, rtol=1e-5)
+    check(torch, c_dp, ref_gemm(torch, a, b))
+
+
+def test_gemm_workspace_too_small_is_rejected(torch_cuda):
+    torch = torch_cuda
+    from ntilang_b200 import _lib
+
+    m = n = k = 4096
+    need = _lib.gemm_workspace_size(m, n, k, 0)
+    a = torch.zeros(m, k, device="cuda").half()
+    b = torch.zeros(k, n, device="cuda").half()
+    c = torch.empty(m, n, device="cuda")
+    ws = torch.zeros(need // 2, dtype=torch.uint8, device="cuda")
+    with pytest.raises(_lib.KernelError, match="workspace"):
+        _lib.call("ntl_gemm_f16_f32_ws", a.data_ptr(), b.data_ptr(), c.data_ptr(), None, 0, 1.0, 0, m, n, k, 0,
+                  ws.data_ptr(), ws.numel(), torch.cuda.current_stream().cuda_stream)
