@@ -313,14 +313,15 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_tc_kernel(const __grid_consta
       const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + acc * BN;
       if (w.k0 > 0) {
         // Stream-K contributor: raw partial sums -> this CTA's workspace slot, then its flag.
-        float* slot = p.ws + static_cast<size_t>(blockIdx.x) * SK_SLOT_FLOATS + static_cast<size_t>(r_local) * BN;
+        // Slot layout [column quad][row][4]: a warp's float4 stores are 512 contiguous bytes.
+        float4* slot = reinterpret_cast<float4*>(p.ws + static_cast<size_t>(blockIdx.x) * SK_SLOT_FLOATS) + r_local;
         for (int chunk = 0; chunk < BN / 32; ++chunk) {
           uint32_t r[32];
           tmem_ld_32x32b_x32(t_row + chunk * 32, r);
           tc_wait_ld();
 #pragma unroll
           for (int j = 0; j < 32; j += 4)
-            __stcg(reinterpret_cast<float4*>(slot + chunk * 32 + j),
+            __stcg(slot + static_cast<size_t>(chunk * 8 + j / 4) * BM,
                    make_float4(__uint_as_float(r[j]), __uint_as_float(r[j + 1]), __uint_as_float(r[j + 2]),
                                __uint_as_float(r[j + 3])));
         }
@@ -371,10 +372,10 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_tc_kernel(const __grid_consta
 #pragma unroll
         for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
         for (int cc = first_c; cc <= last_c; ++cc) {
-          const float* part = p.ws + static_cast<size_t>(cc) * SK_SLOT_FLOATS + static_cast<size_t>(r_local) * BN + chunk * 32;
+          const float4* part = reinterpret_cast<const float4*>(p.ws + static_cast<size_t>(cc) * SK_SLOT_FLOATS) + r_local;
 #pragma unroll
           for (int j = 0; j < 32; j += 4) {
-            const float4 q = __ldcg(reinterpret_cast<const float4*>(part + j));
+            const float4 q = __ldcg(part + static_cast<size_t>(chunk * 8 + j / 4) * BM);
             v[j] += q.x, v[j + 1] += q.y, v[j + 2] += q.z, v[j + 3] += q.w;
           }
         }
