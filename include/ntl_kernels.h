@@ -103,6 +103,18 @@ int ntl_gemm_f16_f32_ws(const uint16_t* a, const uint16_t* b, float* c, const fl
                         float alpha, int relu, int64_t M, int64_t N, int64_t K, int b_trans, void* workspace,
                         uint64_t workspace_bytes, ntl_stream_t stream);
 
+/* ntl_gemm_f16_f32_ws for callers that cannot allocate device memory (e.g. a plugin host
+ * that passes only tensors and a stream, or a runtime with the device allocator switched
+ * off): the stream-K scratch lives in a 16 MiB file-scope device array that every GPU
+ * loading the library holds until exit.  Shapes whose plan needs more scratch than that
+ * return NTL_ERR_UNSUPPORTED.  The first call on a device looks up the array's device
+ * address (cudaGetSymbolAddress) and should come before any stream capture.  Calls share
+ * the array: flags are cleared on the caller's stream before each launch, and calls that
+ * overlap on the GPU race.  No counterpart in the reference (its kernels take no scratch). */
+int ntl_gemm_f16_f32_noalloc(const uint16_t* a, const uint16_t* b, float* c, const float* bias, int bias_mode,
+                             float alpha, int relu, int64_t M, int64_t N, int64_t K, int b_trans,
+                             ntl_stream_t stream);
+
 /* FlashAttention-2 forward, fp16 Q,K,V,O [batch, heads, seq, dim] row-major.
  *   O = softmax_base2((Q K^T) * scale_log2 [causal: key <= query]) V, with P rounded to fp16
  *   before the P V product and fp32 softmax statistics.

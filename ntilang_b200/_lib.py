@@ -35,6 +35,9 @@ SIGNATURES = {
     "ntl_gemm_f16_f32_ws": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, c_f32p, c_f32p, ctypes.c_int,
                                            ctypes.c_float, ctypes.c_int, c_i64, c_i64, c_i64, ctypes.c_int,
                                            ctypes.c_void_p, ctypes.c_uint64, ctypes.c_void_p]),
+    "ntl_gemm_f16_f32_noalloc": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, c_f32p, c_f32p, ctypes.c_int,
+                                                ctypes.c_float, ctypes.c_int, c_i64, c_i64, c_i64, ctypes.c_int,
+                                                ctypes.c_void_p]),
     "ntl_fa2_fwd_f16": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, c_i64,
                                        c_i64, c_i64, c_i64, ctypes.c_float, ctypes.c_int, ctypes.c_void_p]),
     "ntl_device_status": (ctypes.c_int, [ctypes.POINTER(ctypes.c_uint32)]),

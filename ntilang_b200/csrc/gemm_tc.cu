@@ -653,3 +653,68 @@ extern "C" int ntl_gemm_f16_f32_ws(const uint16_t* a, const uint16_t* b, float* 
   return gemm_launch(a, b, c, bias, bias_mode, alpha, relu, M, N, K, b_trans, workspace, workspace_bytes, true,
                      static_cast<cudaStream_t>(stream));
 }
+
+// ----------------------------------------------------------------- allocation-free variant
+//
+// Some callers cannot allocate device memory for a workspace: a plugin host that hands a
+// kernel only its tensors and a stream (the reference's TVM-FFI launch path, for one, has no
+// workspace argument), or a runtime that runs with the device allocator switched off after
+// start-up.  ntl_gemm_f16_f32_noalloc gives them the stream-K GEMM with its scratch in a
+// file-scope device array instead of a caller buffer.
+//
+// The array is a fixed 16 MiB that every GPU loading this library holds until the process
+// exits.  Shapes whose stream-K plan needs more (4096^3 on a 148-SM B200 needs ~19 MB) are
+// rejected with NTL_ERR_UNSUPPORTED.  All calls share the array: the flag words are cleared
+// (cudaMemsetAsync on the caller's stream) before every launch, and calls that overlap on
+// the GPU race on it.  Host code cannot pass the array's name to a kernel (on the host it
+// is a stand-in, not a device address), so the first call on each device looks up its
+// device address with cudaGetSymbolAddress while that device is current; make that first
+// call before any stream capture.  Nothing here allocates.
+constexpr size_t kNoAllocScratchBytes = size_t(16) << 20;
+static __device__ __align__(256) unsigned char g_gemm_noalloc_scratch[kNoAllocScratchBytes];
+
+namespace {
+std::mutex g_scratch_mu;
+void* g_scratch_ptr[64] = {};
+
+int noalloc_scratch(void** out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return ntl_fail(NTL_ERR_CUDA, "cudaGetDevice failed");
+  if (dev < 0 || dev >= 64) return ntl_fail(NTL_ERR_UNSUPPORTED, "gemm_noalloc: device index %d out of range", dev);
+  std::lock_guard<std::mutex> lock(g_scratch_mu);
+  if (g_scratch_ptr[dev] == nullptr) {
+    void* ptr = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&ptr, g_gemm_noalloc_scratch);
+    if (e != cudaSuccess || ptr == nullptr)
+      return ntl_fail(NTL_ERR_CUDA, "gemm_noalloc: cudaGetSymbolAddress failed: %s", cudaGetErrorString(e));
+    g_scratch_ptr[dev] = ptr;
+  }
+  *out = g_scratch_ptr[dev];
+  return NTL_OK;
+}
+}  // namespace
+
+extern "C" int ntl_gemm_f16_f32_noalloc(const uint16_t* a, const uint16_t* b, float* c, const float* bias,
+                                        int bias_mode, float alpha, int relu, int64_t M, int64_t N, int64_t K,
+                                        int b_trans, ntl_stream_t stream) {
+  uint64_t need = 0;
+  if (int rc = ntl_gemm_workspace_size(M, N, K, b_trans, &need)) return rc;
+  NTL_REQUIRE(need <= kNoAllocScratchBytes, NTL_ERR_UNSUPPORTED,
+              "gemm_noalloc: this shape needs %llu bytes of scratch, more than the %zu-byte static maximum "
+              "(use ntl_gemm_f16_f32_ws with a caller workspace)",
+              (unsigned long long)need, kNoAllocScratchBytes);
+  void* scratch = nullptr;
+  if (int rc = noalloc_scratch(&scratch)) return rc;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (need > 0) {
+    // The plan's flag words follow its partial-sum slots; they must start at zero.
+    Plan pl;
+    if (int rc = make_plan(M, N, K, true, &pl)) return rc;
+    const size_t flags_off = static_cast<size_t>(pl.sk_ctas) * SK_SLOT_FLOATS * sizeof(float);
+    cudaError_t e = cudaMemsetAsync(static_cast<unsigned char*>(scratch) + flags_off, 0,
+                                    static_cast<size_t>(pl.sk_ctas) * 4, s);
+    if (e != cudaSuccess) return ntl_fail(NTL_ERR_CUDA, "gemm_noalloc: clearing flags: %s", cudaGetErrorString(e));
+  }
+  return gemm_launch(a, b, c, bias, bias_mode, alpha, relu, M, N, K, b_trans, need > 0 ? scratch : nullptr,
+                     need > 0 ? kNoAllocScratchBytes : 0, true, s);
+}
