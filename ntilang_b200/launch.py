@@ -68,11 +68,11 @@ def launch(spec: OpSpec, tensors, stream: int) -> None:
         bias = tensors[a["bias"]] if "bias" in a else None
         M, K = int(A.shape[0]), int(A.shape[1])
         N = int(B.shape[0]) if p["transpose_b"] else int(B.shape[1])
-        nbytes = _lib.gemm_workspace_size(M, N, K, int(p["transpose_b"]))
-        ws = gemm_workspace(A.device, nbytes) if nbytes else None
-        _lib.call("ntl_gemm_f16_f32_ws", _ptr(A), _ptr(B), _ptr(C), _ptr(bias) if bias is not None else None,
-                  int(p["bias_mode"]), float(p["alpha"]), int(p["relu"]), M, N, K, int(p["transpose_b"]),
-                  _ptr(ws) if ws is not None else None, ws.numel() if ws is not None else 0, stream)
+        # Data-parallel tiles: on B200 the stream-K split of the last wave (ntl_gemm_f16_f32_ws)
+        # measured slower for every shape tried (the mainloop is bound by L2->SM bandwidth,
+        # which stream-K spreads over more SMs without reducing).
+        _lib.call("ntl_gemm_f16_f32", _ptr(A), _ptr(B), _ptr(C), _ptr(bias) if bias is not None else None,
+                  int(p["bias_mode"]), float(p["alpha"]), int(p["relu"]), M, N, K, int(p["transpose_b"]), stream)
     elif f == "fa2":
         q, k, v, o = tensors[a["q"]], tensors[a["k"]], tensors[a["v"]], tensors[a["o"]]
         b, h, s, d = (int(x) for x in q.shape)
@@ -87,7 +87,7 @@ ABI_CALL = {
     "cumsum": "ntl_cumsum_f32(X, Y, rows, cols, reverse, stream)",
     "softmax": "ntl_softmax_f32(X, Y, rows, cols, stream)",
     "rmsnorm": "ntl_rmsnorm_f32(X, W, Y, rows, cols, eps, inv_n, stream)",
-    "gemm": "ntl_gemm_f16_f32_ws(A, B, C, bias, bias_mode, alpha, relu, M, N, K, b_trans, workspace, bytes, stream)",
+    "gemm": "ntl_gemm_f16_f32(A, B, C, bias, bias_mode, alpha, relu, M, N, K, b_trans, stream)",
     "fa2": "ntl_fa2_fwd_f16(Q, K, V, O, batch, heads, seq, dim, scale_log2, causal, stream)",
 }
 

@@ -154,15 +154,20 @@ def test_gemm_stream_k_repeated_calls(torch_cuda, m, n, k):
     torch = torch_cuda
     from ntilang_b200 import _lib
 
-    assert _lib.gemm_workspace_size(m, n, k, 0) > 0
+    from ntilang_b200.launch import gemm_workspace
+
+    need = _lib.gemm_workspace_size(m, n, k, 0)
+    assert need > 0
+    ws = gemm_workspace(torch.device("cuda"), need)
     gen = torch.Generator(device="cuda").manual_seed(m + k)
     a = (torch.randn(m, k, device="cuda", generator=gen) / k**0.5).half()
     b = torch.randn(k, n, device="cuda", generator=gen).half()
     bias = torch.randn(n, device="cuda", generator=gen) * 0.1
-    kern = K.matmul_bias_relu(m, n, k)
     ref = torch.relu(ref_gemm(torch, a, b) + bias)
     for _ in range(3):
-        c = kern(a, b, bias)
+        c = torch.full((m, n), float("nan"), device="cuda")
+        _lib.call("ntl_gemm_f16_f32_ws", a.data_ptr(), b.data_ptr(), c.data_ptr(), bias.data_ptr(), 1, 1.0, 1, m, n,
+                  k, 0, ws.data_ptr(), ws.numel(), torch.cuda.current_stream().cuda_stream)
         check(torch, c, ref)
 
 
@@ -173,10 +178,15 @@ def test_gemm_stream_k_matches_data_parallel_entry(torch_cuda):
     m = n = k = 2048
     a = torch.randn(m, k, device="cuda").half()
     b = torch.randn(k, n, device="cuda").half()
+    from ntilang_b200.launch import gemm_workspace
+
     c_dp = torch.empty(m, n, device="cuda")
+    c_sk = torch.empty(m, n, device="cuda")
     s = torch.cuda.current_stream().cuda_stream
+    ws = gemm_workspace(torch.device("cuda"), _lib.gemm_workspace_size(m, n, k, 0))
     _lib.call("ntl_gemm_f16_f32", a.data_ptr(), b.data_ptr(), c_dp.data_ptr(), None, 0, 1.0, 0, m, n, k, 0, s)
-    c_sk = K.matmul(m, n, k)(a, b)
+    _lib.call("ntl_gemm_f16_f32_ws", a.data_ptr(), b.data_ptr(), c_sk.data_ptr(), None, 0, 1.0, 0, m, n, k, 0,
+              ws.data_ptr(), ws.numel(), s)
     check(torch, c_sk, c_dp, rtol=1e-5)
     check(torch, c_dp, ref_gemm(torch, a, b))
 
