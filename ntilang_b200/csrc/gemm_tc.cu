@@ -135,6 +135,29 @@ __device__ __forceinline__ float epi(float acc, float alpha, float b, int relu, 
   return relu ? fmaxf(v, 0.0f) : v;
 }
 
+// Epilogue of 32 accumulator columns [col0, col0+32) of one output row: alpha, bias, ReLU,
+// then 128-bit stores when the row is 16-byte aligned and the chunk lies inside C.
+__device__ __forceinline__ void store_row_chunk(float (&v)[32], const GemmParams& p, int row, int col0, float* crow,
+                                                float row_bias) {
+#pragma unroll
+  for (int j = 0; j < 32; ++j) {
+    float b = row_bias;
+    const int col = col0 + j;
+    if (p.bias_mode == NTL_BIAS_N) b = (col < p.N) ? __ldg(p.bias + col) : 0.0f;
+    else if (p.bias_mode == NTL_BIAS_MN) b = (col < p.N) ? __ldg(p.bias + static_cast<int64_t>(row) * p.N + col) : 0.0f;
+    v[j] = epi(v[j], p.alpha, b, p.relu, p.bias_mode);
+  }
+  if (p.vec_store && col0 + 32 <= p.N) {
+#pragma unroll
+    for (int j = 0; j < 32; j += 4)
+      *reinterpret_cast<float4*>(crow + col0 + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+  } else {
+#pragma unroll
+    for (int j = 0; j < 32; ++j)
+      if (col0 + j < p.N) crow[col0 + j] = v[j];
+  }
+}
+
 __device__ __forceinline__ uint32_t ld_acquire_u32(const uint32_t* p) {
   uint32_t v;
   asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
@@ -283,12 +306,11 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_tc_kernel(const __grid_consta
         if (!ok) break;
         tc_commit(&ctl->acc_full[acc]);
       }
-      if (!ok) {
-        // Drain: wait until every MMA this thread issued has retired before TMEM is freed.
-        tc_commit(&ctl->drain);
-        if (!mbar_wait_bounded(&ctl->drain, 0, int64_t(1) << 24, nullptr))
-          atomicCAS(&g_gemm_status, 0u, NTL_STATUS_DRAIN_WAIT);
-      }
+      // Drain: every MMA this thread issued retires before TMEM is freed, also when another
+      // role gave up after the last issue.
+      tc_commit(&ctl->drain);
+      if (!mbar_wait_bounded(&ctl->drain, 0, int64_t(1) << 24, nullptr))
+        atomicCAS(&g_gemm_status, 0u, NTL_STATUS_DRAIN_WAIT);
     }
   } else {
     // ------------------------------------------------------------ epilogue (warps 2..5)
@@ -381,23 +403,7 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_tc_kernel(const __grid_consta
         }
         const int col0 = nb * BN + chunk * 32;
         if (!row_ok || col0 >= p.N) continue;
-#pragma unroll
-        for (int j = 0; j < 32; ++j) {
-          float b = row_bias;
-          const int col = col0 + j;
-          if (p.bias_mode == NTL_BIAS_N) b = (col < p.N) ? __ldg(p.bias + col) : 0.0f;
-          else if (p.bias_mode == NTL_BIAS_MN) b = (col < p.N) ? __ldg(p.bias + static_cast<int64_t>(row) * p.N + col) : 0.0f;
-          v[j] = epi(v[j], p.alpha, b, p.relu, p.bias_mode);
-        }
-        if (p.vec_store && col0 + 32 <= p.N) {
-#pragma unroll
-          for (int j = 0; j < 32; j += 4)
-            *reinterpret_cast<float4*>(crow + col0 + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
-        } else {
-#pragma unroll
-          for (int j = 0; j < 32; ++j)
-            if (col0 + j < p.N) crow[col0 + j] = v[j];
-        }
+        store_row_chunk(v, p, row, col0, crow, row_bias);
       }
       tc_fence_before();
       __syncwarp();
@@ -420,6 +426,240 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_tc_kernel(const __grid_consta
   __syncthreads();
   tc_fence_after();
   if (warp == 1) tmem_dealloc(tmem_base, TMEM_COLS);
+}
+
+// ------------------------------------------------------------------ CTA-pair kernel
+// The same GEMM on clusters of two CTAs (two SMs) that share one tcgen05 MMA of
+// M=256 x N=256 x K=16 (cta_group::2).  The even CTA (rank 0) issues the MMAs; each CTA
+// holds 128 rows of the pair's A tile and 128 columns of its B tile in its own shared
+// memory, and 128 rows x 256 columns of the accumulator in its own TMEM.  Per k-block an SM
+// loads 32 KB instead of the 48 KB of the one-SM kernel for the same tensor work, which is
+// what bounds that kernel (its loads from L2 run at the SM's operand bandwidth).
+//   warp 0 (both CTAs)  TMA: own A rows and own B columns; completion is counted on the
+//                       even CTA's `full` barrier, which that CTA arms for both halves.
+//   warp 1 (rank 0)     MMA issue; commits release `empty` and signal `acc_full` in both
+//                       CTAs (commit multicast, no multicast loads).
+//   warps 2..5          epilogue of the CTA's 128 rows; they free an accumulator by
+//                       arriving on the even CTA's `acc_empty` (8 arrivals).
+// Teardown: both CTAs meet at a cluster barrier; if any role gave up, the even CTA's
+// producer balances and waits out every stage load either CTA still has in flight (it knows
+// both issue counts), then both meet again before TMEM is freed.
+constexpr int PR_TILE_M = 256;                   // rows of a pair tile (128 per CTA)
+constexpr int PR_BM = 128;
+constexpr int PR_BN_HALF = BN / 2;               // B columns held by one CTA
+constexpr int PR_STAGES = 6;
+constexpr int PR_A_STAGE = PR_BM * BK * 2;       // 16 KB
+constexpr int PR_B_STAGE = PR_BN_HALF * BK * 2;  // 16 KB
+constexpr int PR_STAGE_BYTES = PR_A_STAGE + PR_B_STAGE;
+constexpr int PR_SMEM_BYTES = PR_STAGES * PR_STAGE_BYTES + 1024 + 1024;
+static_assert(PR_SMEM_BYTES <= 227 * 1024, "pair kernel shared memory");
+
+struct __align__(8) PairCtl {
+  uint64_t full[PR_STAGES];   // rank 0: both CTAs' loads of a stage landed
+  uint64_t empty[PR_STAGES];  // each CTA: the MMAs reading the stage retired
+  uint64_t acc_full[2];       // each CTA: accumulator complete
+  uint64_t acc_empty[2];      // rank 0: the 8 epilogue warps of the pair drained it
+  uint64_t drain;
+  uint32_t tmem_base;
+  int abort;
+  int issued;       // rank 0: stage loads its producer issued
+  int peer_issued;  // rank 0: stage loads the odd CTA's producer issued
+};
+
+__device__ __forceinline__ void pair_abort(PairCtl* ctl, uint32_t code) {
+  atomicCAS(&g_gemm_status, 0u, code);
+  *reinterpret_cast<volatile int*>(&ctl->abort) = 1;
+  st_cluster_s32(mapa_shared(smem_u32(&ctl->abort), cluster_ctarank() ^ 1u), 1);
+}
+
+__global__ void __launch_bounds__(THREADS, 1) gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a,
+                                                               const __grid_constant__ CUtensorMap tmap_b,
+                                                               const GemmParams p) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + PR_STAGES * PR_A_STAGE;
+  PairCtl* ctl = reinterpret_cast<PairCtl*>(smem + PR_STAGES * PR_STAGE_BYTES);
+  volatile int* abort_flag = &ctl->abort;
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const int pair = blockIdx.x >> 1;
+  const int num_pairs = gridDim.x >> 1;
+  const int tiles = p.num_m * p.num_n;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < PR_STAGES; ++s) {
+      mbar_init(&ctl->full[s], 1);
+      mbar_init(&ctl->empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&ctl->acc_full[a], 1);
+      mbar_init(&ctl->acc_empty[a], 8);
+    }
+    mbar_init(&ctl->drain, 1);
+    ctl->abort = 0;
+    ctl->issued = 0;
+    ctl->peer_issued = 0;
+    fence_mbar_init();
+    prefetch_tensormap(&tmap_a);
+    prefetch_tensormap(&tmap_b);
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(&ctl->tmem_base, TMEM_COLS);
+    tmem_relinquish_pair();
+  }
+  // Barriers initialised and TMEM allocated in both CTAs before any cross-CTA signal.
+  tc_fence_before();
+  cluster_sync_all();
+  tc_fence_after();
+  const uint32_t tmem_base = ctl->tmem_base;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ TMA producer (both CTAs)
+    if (elect_one_lane()) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int issued = 0;
+      for (int t = pair; t < tiles; t += num_pairs) {
+        int mb, nb;
+        tile_coords(t, p.num_m, p.num_n, mb, nb);
+        const int m0 = mb * PR_TILE_M + static_cast<int>(rank) * PR_BM;
+        const int n0 = nb * BN + static_cast<int>(rank) * PR_BN_HALF;
+        bool ok = true;
+        for (int kb = 0; kb < p.kb; ++kb) {
+          if (!mbar_wait_bounded(&ctl->empty[stage], phase ^ 1, p.wait_limit, abort_flag)) {
+            if (!*abort_flag) pair_abort(ctl, NTL_STATUS_TMA_EMPTY_WAIT);
+            ok = false;
+            break;
+          }
+          const uint32_t full_addr = mapa_shared(smem_u32(&ctl->full[stage]), 0);
+          if (rank == 0) mbar_arrive_expect_tx(&ctl->full[stage], 2 * PR_STAGE_BYTES);
+          uint8_t* a_dst = sA + stage * PR_A_STAGE;
+          uint8_t* b_dst = sB + stage * PR_B_STAGE;
+          tma_load_2d_pair(a_dst, &tmap_a, full_addr, kb * BK, m0);
+          if (p.b_trans) {
+            tma_load_2d_pair(b_dst, &tmap_b, full_addr, kb * BK, n0);
+          } else {
+#pragma unroll
+            for (int i = 0; i < PR_BN_HALF / 64; ++i)
+              tma_load_2d_pair(b_dst + i * (64 * BK * 2), &tmap_b, full_addr, n0 + i * 64, kb * BK);
+          }
+          ++issued;
+          if (++stage == PR_STAGES) stage = 0, phase ^= 1;
+        }
+        if (!ok) break;
+      }
+      if (rank == 0) ctl->issued = issued;
+      else st_cluster_s32(mapa_shared(smem_u32(&ctl->peer_issued), 0), issued);
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer (rank 0)
+    if (rank == 0 && elect_one_lane()) {
+      const uint32_t idesc = umma_idesc_f16_f32(PR_TILE_M, BN, 0, p.b_trans ? 0 : 1);
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      int local = 0;
+      for (int t = pair; ok && t < tiles; t += num_pairs, ++local) {
+        const int acc = local & 1;
+        const uint32_t acc_phase = (local >> 1) & 1;
+        if (!mbar_wait_bounded(&ctl->acc_empty[acc], acc_phase ^ 1, p.wait_limit, abort_flag)) {
+          if (!*abort_flag) pair_abort(ctl, NTL_STATUS_ACC_EMPTY_WAIT);
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * BN;
+        for (int kb = 0; kb < p.kb; ++kb) {
+          if (!mbar_wait_bounded(&ctl->full[stage], phase, p.wait_limit, abort_flag)) {
+            if (!*abort_flag) pair_abort(ctl, NTL_STATUS_MMA_FULL_WAIT);
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(sA + stage * PR_A_STAGE);
+          const uint32_t b_addr = smem_u32(sB + stage * PR_B_STAGE);
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k) {
+            const uint64_t adesc = umma_desc_sw128(a_addr + k * 32, 16, 1024);
+            const uint64_t bdesc = p.b_trans ? umma_desc_sw128(b_addr + k * 32, 16, 1024)
+                                             : umma_desc_sw128(b_addr + k * 2048, 64 * BK * 2, 1024);
+            tc_mma_f16_ss_pair(d_tmem, adesc, bdesc, idesc, (kb > 0 || k > 0) ? 1u : 0u);
+          }
+          tc_commit_pair_mc(&ctl->empty[stage], 0x3);
+          if (++stage == PR_STAGES) stage = 0, phase ^= 1;
+        }
+        if (!ok) break;
+        tc_commit_pair_mc(&ctl->acc_full[acc], 0x3);
+      }
+      // Every MMA issued retires before TMEM is freed.
+      tc_commit_pair(&ctl->drain);
+      if (!mbar_wait_bounded(&ctl->drain, 0, int64_t(1) << 24, nullptr))
+        atomicCAS(&g_gemm_status, 0u, NTL_STATUS_DRAIN_WAIT);
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue (warps 2..5, both CTAs)
+    const int quarter = warp & 3;
+    const int r_local = quarter * 32 + lane;
+    const uint32_t t_lane = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16);
+    int local = 0;
+    for (int t = pair; t < tiles; t += num_pairs, ++local) {
+      int mb, nb;
+      tile_coords(t, p.num_m, p.num_n, mb, nb);
+      const int acc = local & 1;
+      const uint32_t acc_phase = (local >> 1) & 1;
+      if (!mbar_wait_bounded(&ctl->acc_full[acc], acc_phase, p.wait_limit, abort_flag)) {
+        if (!*abort_flag) pair_abort(ctl, NTL_STATUS_ACC_FULL_WAIT);
+        break;
+      }
+      __syncwarp();
+      tc_fence_after();
+      const int row = mb * PR_TILE_M + static_cast<int>(rank) * PR_BM + r_local;
+      const bool row_ok = row < p.M;
+      float* crow = p.c + static_cast<int64_t>(row) * p.N;
+      const float row_bias = (p.bias_mode == NTL_BIAS_M && row_ok) ? __ldg(p.bias + row) : 0.0f;
+      for (int chunk = 0; chunk < BN / 32; ++chunk) {
+        const int col0 = nb * BN + chunk * 32;
+        if (col0 >= p.N) break;
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(t_lane + acc * BN + chunk * 32, r);
+        tc_wait_ld();
+        if (!row_ok) continue;
+        float v[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+        store_row_chunk(v, p, row, col0, crow, row_bias);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_u32(&ctl->acc_empty[acc]), 0));
+    }
+  }
+
+  // ------------------------------------------------------------ teardown
+  tc_fence_before();
+  cluster_sync_all();
+  if (rank == 0 && threadIdx.x == 0 && *abort_flag) {
+    // Stage loads of either CTA may still be in flight; they all count on this CTA's `full`
+    // barriers.  Sequences below min(issued) are armed for both halves; between the two
+    // counts one half is missing: arm the odd CTA's half, or retire the half that will not
+    // come.  Then wait each barrier's pending phase (the last PR_STAGES sequences cover
+    // every load not yet consumed).
+    const int own = ctl->issued, peer = ctl->peer_issued;
+    const int hi = own > peer ? own : peer;
+    for (int i = hi > PR_STAGES ? hi - PR_STAGES : 0; i < hi; ++i) {
+      const int s = i % PR_STAGES;
+      const uint32_t ph = static_cast<uint32_t>(i / PR_STAGES) & 1u;
+      if (i >= own) mbar_arrive_expect_tx(&ctl->full[s], PR_STAGE_BYTES);
+      else if (i >= peer) mbar_complete_tx(&ctl->full[s], PR_STAGE_BYTES);
+      if (!mbar_wait_bounded(&ctl->full[s], ph, int64_t(1) << 24, nullptr))
+        atomicCAS(&g_gemm_status, 0u, NTL_STATUS_DRAIN_WAIT);
+    }
+  }
+  cluster_sync_all();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc_pair(tmem_base, TMEM_COLS);
 }
 
 // ------------------------------------------------------------------ CUDA-core fallback
@@ -525,6 +765,73 @@ int ensure_smem_attr() {
   return NTL_OK;
 }
 
+// The pair kernel's shared-memory opt-in and how many 2-CTA clusters fit on the device at
+// once (its persistent grid), cached per device.
+int pair_clusters(int* clusters_out) {
+  static std::atomic<int> cached[64] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return ntl_fail(NTL_ERR_CUDA, "cudaGetDevice failed");
+  if (dev >= 0 && dev < 64) {
+    const int c = cached[dev].load(std::memory_order_acquire);
+    if (c > 0) {
+      *clusters_out = c;
+      return NTL_OK;
+    }
+  }
+  cudaError_t e = cudaFuncSetAttribute(gemm_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, PR_SMEM_BYTES);
+  if (e != cudaSuccess) return ntl_fail(NTL_ERR_CUDA, "cudaFuncSetAttribute(gemm pair): %s", cudaGetErrorString(e));
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(2, 1, 1);
+  cfg.blockDim = dim3(THREADS, 1, 1);
+  cfg.dynamicSmemBytes = PR_SMEM_BYTES;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2, attr[0].val.clusterDim.y = 1, attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  int clusters = 0;
+  e = cudaOccupancyMaxActiveClusters(&clusters, gemm_pair_kernel, &cfg);
+  if (e != cudaSuccess || clusters < 1)
+    return ntl_fail(NTL_ERR_CUDA, "cudaOccupancyMaxActiveClusters(gemm pair): %s", cudaGetErrorString(e));
+  if (dev >= 0 && dev < 64) cached[dev].store(clusters, std::memory_order_release);
+  *clusters_out = clusters;
+  return NTL_OK;
+}
+
+int gemm_pair_launch(const uint16_t* a, const uint16_t* b, GemmParams p, cudaStream_t s) {
+  int clusters = 0;
+  if (int rc = pair_clusters(&clusters)) return rc;
+  p.num_m = static_cast<int>((p.M + PR_TILE_M - 1) / PR_TILE_M);
+  p.num_n = static_cast<int>((p.N + BN - 1) / BN);
+  p.kb = static_cast<int>((p.K + BK - 1) / BK);
+  const int64_t tiles = static_cast<int64_t>(p.num_m) * p.num_n;
+  NTL_REQUIRE(tiles < (int64_t(1) << 31), NTL_ERR_UNSUPPORTED, "gemm: too many tiles");
+  p.dp_tiles = static_cast<int>(tiles);
+  p.sk_ctas = 0, p.sk_units = 0, p.ws = nullptr, p.flags = nullptr;
+  CUtensorMap ma, mb;
+  if (int rc = make_map_f16(&ma, a, p.M, p.K, BK, PR_BM)) return rc;
+  if (p.b_trans) {
+    if (int rc = make_map_f16(&mb, b, p.N, p.K, BK, PR_BN_HALF)) return rc;
+  } else {
+    if (int rc = make_map_f16(&mb, b, p.K, p.N, 64, BK)) return rc;
+  }
+  const int pairs = static_cast<int>(tiles < clusters ? tiles : clusters);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(2 * pairs), 1, 1);
+  cfg.blockDim = dim3(THREADS, 1, 1);
+  cfg.dynamicSmemBytes = PR_SMEM_BYTES;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2, attr[0].val.clusterDim.y = 1, attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, gemm_pair_kernel, ma, mb, p);
+  ntl_note_launch();
+  if (e != cudaSuccess) return ntl_fail(NTL_ERR_CUDA, "gemm (CTA-pair path) launch: %s", cudaGetErrorString(e));
+  return ntl_check_launch("gemm (CTA-pair path) launch");
+}
+
 // Work plan for an M x N x K problem.  Stream-K applies only with a workspace.
 struct Plan {
   int num_m, num_n, tiles, kb, grid, dp_tiles, sk_ctas;
@@ -590,6 +897,7 @@ int gemm_launch(const uint16_t* a, const uint16_t* b, float* c, const float* bia
     ntl_note_launch();
     return ntl_check_launch("gemm (CUDA-core path) launch");
   }
+  if (!stream_k && M > PR_BM) return gemm_pair_launch(a, b, p, s);
   Plan pl;
   if (int rc = make_plan(M, N, K, stream_k, &pl)) return rc;
   if (pl.sk_ctas > 0) {
