@@ -32,6 +32,8 @@ __global__ void __launch_bounds__(kThreads) binary_f32_v4(const float4* __restri
                                                           float4* __restrict__ c, int64_t n4,
                                                           const float* __restrict__ at, const float* __restrict__ bt,
                                                           float* __restrict__ ct, int tail) {
+  pdl_wait();
+  pdl_trigger();
   const int64_t stride = static_cast<int64_t>(gridDim.x) * kThreads * kUnroll;
   for (int64_t base = static_cast<int64_t>(blockIdx.x) * kThreads * kUnroll + threadIdx.x; base < n4;
        base += stride) {
@@ -58,6 +60,8 @@ template <int OP>
 __global__ void __launch_bounds__(kThreads) binary_f32_scalar(const float* __restrict__ a,
                                                               const float* __restrict__ b, float* __restrict__ c,
                                                               int64_t n) {
+  pdl_wait();
+  pdl_trigger();
   const int64_t stride = static_cast<int64_t>(gridDim.x) * kThreads;
   for (int64_t i = static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x; i < n; i += stride)
     c[i] = apply<OP>(__ldcs(a + i), __ldcs(b + i));
@@ -74,13 +78,13 @@ int launch_binary(const float* a, const float* b, float* c, int64_t n, cudaStrea
     int64_t blocks = (n4 + kThreads * kUnroll - 1) / (kThreads * kUnroll);
     if (blocks > max_blocks) blocks = max_blocks;
     if (blocks < 1) blocks = 1;
-    binary_f32_v4<OP><<<static_cast<unsigned>(blocks), kThreads, 0, stream>>>(
-        reinterpret_cast<const float4*>(a), reinterpret_cast<const float4*>(b), reinterpret_cast<float4*>(c), n4,
-        a + n4 * 4, b + n4 * 4, c + n4 * 4, tail);
+    ntl_launch_pdl(binary_f32_v4<OP>, dim3(static_cast<unsigned>(blocks)), dim3(kThreads), 0, stream,
+                   reinterpret_cast<const float4*>(a), reinterpret_cast<const float4*>(b),
+                   reinterpret_cast<float4*>(c), n4, a + n4 * 4, b + n4 * 4, c + n4 * 4, tail);
   } else {
     int64_t blocks = (n + kThreads - 1) / kThreads;
     if (blocks > max_blocks) blocks = max_blocks;
-    binary_f32_scalar<OP><<<static_cast<unsigned>(blocks), kThreads, 0, stream>>>(a, b, c, n);
+    ntl_launch_pdl(binary_f32_scalar<OP>, dim3(static_cast<unsigned>(blocks)), dim3(kThreads), 0, stream, a, b, c, n);
   }
   ntl_note_launch();
   return ntl_check_launch("elementwise launch");

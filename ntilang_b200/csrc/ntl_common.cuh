@@ -62,6 +62,25 @@ __device__ __forceinline__ bool elect_one_lane() {
   return pred != 0;
 }
 
+// ---- programmatic dependent launch
+// A kernel launched by ntl_launch_pdl may start while the previous kernel on its stream is
+// still running.  It must call pdl_wait() before its first global-memory access: that waits
+// until the previous grid has completed and its writes are visible (it returns at once
+// when there is no such grid).  pdl_trigger() lets the next kernel on the stream start its
+// own launch; it is only a scheduling hint, the next kernel's pdl_wait() still waits for
+// this grid to complete.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+// Hint: bring [p, p + bytes) (whole 16-byte units inside it) into L2.  Safe before pdl_wait():
+// L2 is the device's point of coherence, so a line the previous kernel writes afterwards is
+// updated there, and the loads issued after pdl_wait() see the new data.
+__device__ __forceinline__ void prefetch_l2(const void* p, int64_t bytes) {
+  const uint64_t a = static_cast<uint64_t>(__cvta_generic_to_global(p));
+  const uint64_t s = (a + 15) & ~uint64_t(15);
+  const uint64_t e = (a + static_cast<uint64_t>(bytes)) & ~uint64_t(15);
+  if (e > s) asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(s), "r"(static_cast<uint32_t>(e - s)) : "memory");
+}
+
 // ---- mbarrier
 __device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
   asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
@@ -368,6 +387,24 @@ __device__ __forceinline__ void tc_commit_pair_mc(uint64_t* bar, uint16_t cta_ma
 __device__ __forceinline__ void tc_commit_pair(uint64_t* bar) {
   asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
                : "memory");
+}
+
+// Launch with programmatic stream serialization (see pdl_wait).  Only for kernels that call
+// pdl_wait() before touching global memory.
+template <typename... KArgs, typename... Args>
+cudaError_t ntl_launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                           Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
 }
 
 #endif  // __CUDACC__

@@ -35,6 +35,18 @@ __device__ __forceinline__ void load4(const float* __restrict__ row, int64_t col
   }
 }
 
+// Weights are read by every row: cached loads.
+template <bool VEC>
+__device__ __forceinline__ void load_w4(const float* __restrict__ w, int64_t col, int64_t cols, float (&v)[4]) {
+  if (VEC && col + 3 < cols) {
+    float4 t = __ldg(reinterpret_cast<const float4*>(w + col));
+    v[0] = t.x, v[1] = t.y, v[2] = t.z, v[3] = t.w;
+  } else {
+#pragma unroll
+    for (int e = 0; e < 4; ++e) v[e] = (col + e < cols) ? __ldg(w + col + e) : 0.0f;
+  }
+}
+
 template <bool VEC>
 __device__ __forceinline__ void store4(float* __restrict__ row, int64_t col, int64_t cols, const float (&v)[4]) {
   if (VEC && col + 3 < cols) {
@@ -81,6 +93,9 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32) softmax_rows_warp(const f
                                                                          int64_t cols) {
   const int lane = threadIdx.x & 31;
   const int64_t row = static_cast<int64_t>(blockIdx.x) * kWarpsPerBlock + (threadIdx.x >> 5);
+  if (lane == 0 && row < rows) prefetch_l2(x + row * cols, cols * 4);
+  pdl_wait();
+  pdl_trigger();
   if (row >= rows) return;
   const float* xr = x + row * cols;
   float* yr = y + row * cols;
@@ -117,6 +132,9 @@ __global__ void __launch_bounds__(256) softmax_rows_cta(const float* __restrict_
   __shared__ float red_max[8];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int64_t row = blockIdx.x;
+  if (threadIdx.x == 0) prefetch_l2(x + row * cols, cols < 4096 ? cols * 4 : 16384);  // first 16 KB
+  pdl_wait();
+  pdl_trigger();
   const float* xr = x + row * cols;
   float* yr = y + row * cols;
   float v[NCH][4];
@@ -168,6 +186,10 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32) rmsnorm_rows_warp(const f
                                                                          int64_t cols, float eps, float inv_n) {
   const int lane = threadIdx.x & 31;
   const int64_t row = static_cast<int64_t>(blockIdx.x) * kWarpsPerBlock + (threadIdx.x >> 5);
+  if (lane == 0 && row < rows) prefetch_l2(x + row * cols, cols * 4);
+  if (threadIdx.x == 32) prefetch_l2(w, cols * 4);
+  pdl_wait();
+  pdl_trigger();
   if (row >= rows) return;
   const float* xr = x + row * cols;
   float* yr = y + row * cols;
@@ -188,13 +210,7 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32) rmsnorm_rows_warp(const f
   for (int c = 0; c < NCH; ++c) {
     const int64_t col = static_cast<int64_t>(c) * 128 + lane * 4;
     float wv[4];
-    if (VEC && col + 3 < cols) {
-      float4 t = __ldg(reinterpret_cast<const float4*>(w + col));
-      wv[0] = t.x, wv[1] = t.y, wv[2] = t.z, wv[3] = t.w;
-    } else {
-#pragma unroll
-      for (int e = 0; e < 4; ++e) wv[e] = (col + e < cols) ? __ldg(w + col + e) : 0.0f;
-    }
+    load_w4<VEC>(w, col, cols, wv);
 #pragma unroll
     for (int e = 0; e < 4; ++e) v[c][e] = __fmul_rn(__fmul_rn(v[c][e], inv), wv[e]);
     store4<VEC>(yr, col, cols, v[c]);
@@ -208,6 +224,10 @@ __global__ void __launch_bounds__(256) rmsnorm_rows_cta(const float* __restrict_
   __shared__ float red[NCH][8];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int64_t row = blockIdx.x;
+  if (threadIdx.x == 0) prefetch_l2(x + row * cols, cols < 4096 ? cols * 4 : 16384);  // first 16 KB
+  if (threadIdx.x == 32) prefetch_l2(w, cols * 4);
+  pdl_wait();
+  pdl_trigger();
   const float* xr = x + row * cols;
   float* yr = y + row * cols;
   float v[NCH][4];
@@ -236,13 +256,7 @@ __global__ void __launch_bounds__(256) rmsnorm_rows_cta(const float* __restrict_
   for (int c = 0; c < NCH; ++c) {
     const int64_t col = static_cast<int64_t>(c) * 1024 + threadIdx.x * 4;
     float wv[4];
-    if (VEC && col + 3 < cols) {
-      float4 t = __ldg(reinterpret_cast<const float4*>(w + col));
-      wv[0] = t.x, wv[1] = t.y, wv[2] = t.z, wv[3] = t.w;
-    } else {
-#pragma unroll
-      for (int e = 0; e < 4; ++e) wv[e] = (col + e < cols) ? __ldg(w + col + e) : 0.0f;
-    }
+    load_w4<VEC>(w, col, cols, wv);
 #pragma unroll
     for (int e = 0; e < 4; ++e) v[c][e] = __fmul_rn(__fmul_rn(v[c][e], inv), wv[e]);
     store4<VEC>(yr, col, cols, v[c]);
@@ -264,19 +278,19 @@ struct Dispatch;
       const int64_t blocks = (rows + kWarpsPerBlock - 1) / kWarpsPerBlock;                              \
       NTL_REQUIRE(blocks <= 0x7fffffff, NTL_ERR_UNSUPPORTED, "too many rows");                         \
       dim3 g(static_cast<unsigned>(blocks)), b(kWarpsPerBlock * 32);                                    \
-      if (nch <= 1) KW<1, VEC><<<g, b, 0, s>>>(__VA_ARGS__);                                            \
-      else if (nch <= 2) KW<2, VEC><<<g, b, 0, s>>>(__VA_ARGS__);                                       \
-      else if (nch <= 4) KW<4, VEC><<<g, b, 0, s>>>(__VA_ARGS__);                                       \
-      else if (nch <= 8) KW<8, VEC><<<g, b, 0, s>>>(__VA_ARGS__);                                       \
-      else KW<16, VEC><<<g, b, 0, s>>>(__VA_ARGS__);                                                    \
+      if (nch <= 1) ntl_launch_pdl(KW<1, VEC>, g, b, 0, s, __VA_ARGS__);                                \
+      else if (nch <= 2) ntl_launch_pdl(KW<2, VEC>, g, b, 0, s, __VA_ARGS__);                           \
+      else if (nch <= 4) ntl_launch_pdl(KW<4, VEC>, g, b, 0, s, __VA_ARGS__);                           \
+      else if (nch <= 8) ntl_launch_pdl(KW<8, VEC>, g, b, 0, s, __VA_ARGS__);                           \
+      else ntl_launch_pdl(KW<16, VEC>, g, b, 0, s, __VA_ARGS__);                                        \
     } else {                                                                                            \
       NTL_REQUIRE(rows <= 0x7fffffff, NTL_ERR_UNSUPPORTED, "too many rows");                           \
       const int64_t cch = (cols + 1023) / 1024;                                                         \
       dim3 g(static_cast<unsigned>(rows)), b(256);                                                      \
-      if (cch <= 2) KC<2, VEC><<<g, b, 0, s>>>(__VA_ARGS__);                                            \
-      else if (cch <= 4) KC<4, VEC><<<g, b, 0, s>>>(__VA_ARGS__);                                       \
-      else if (cch <= 8) KC<8, VEC><<<g, b, 0, s>>>(__VA_ARGS__);                                       \
-      else KC<16, VEC><<<g, b, 0, s>>>(__VA_ARGS__);                                                    \
+      if (cch <= 2) ntl_launch_pdl(KC<2, VEC>, g, b, 0, s, __VA_ARGS__);                                \
+      else if (cch <= 4) ntl_launch_pdl(KC<4, VEC>, g, b, 0, s, __VA_ARGS__);                           \
+      else if (cch <= 8) ntl_launch_pdl(KC<8, VEC>, g, b, 0, s, __VA_ARGS__);                           \
+      else ntl_launch_pdl(KC<16, VEC>, g, b, 0, s, __VA_ARGS__);                                        \
     }                                                                                                   \
   } while (0)
 

@@ -143,6 +143,9 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32) cumsum_rows_reg(const flo
                                                                        int64_t cols) {
   const int lane = threadIdx.x & 31;
   const int64_t row = static_cast<int64_t>(blockIdx.x) * kWarpsPerBlock + (threadIdx.x >> 5);
+  if (lane == 0 && row < rows) prefetch_l2(x + row * cols, cols * 4);
+  pdl_wait();
+  pdl_trigger();
   if (row >= rows) return;
   const float* xr = x + row * cols;
   float* yr = y + row * cols;
@@ -175,6 +178,9 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32) cumsum_rows_loop(const fl
   constexpr int G = 8;
   const int lane = threadIdx.x & 31;
   const int64_t row = static_cast<int64_t>(blockIdx.x) * kWarpsPerBlock + (threadIdx.x >> 5);
+  if (lane == 0 && row < rows) prefetch_l2(x + row * cols, 4096);  // the first group of chunks
+  pdl_wait();
+  pdl_trigger();
   if (row >= rows) return;
   const float* xr = x + row * cols;
   float* yr = y + row * cols;
@@ -208,15 +214,15 @@ int launch(const float* x, float* y, int64_t rows, int64_t cols, cudaStream_t s)
   dim3 grid(static_cast<unsigned>(blocks)), block(kWarpsPerBlock * 32);
   const int64_t nch = (cols + 127) / 128;
   if (nch <= 1)
-    cumsum_rows_reg<1, REV, VEC><<<grid, block, 0, s>>>(x, y, rows, cols);
+    ntl_launch_pdl(cumsum_rows_reg<1, REV, VEC>, grid, block, 0, s, x, y, rows, cols);
   else if (nch <= 2)
-    cumsum_rows_reg<2, REV, VEC><<<grid, block, 0, s>>>(x, y, rows, cols);
+    ntl_launch_pdl(cumsum_rows_reg<2, REV, VEC>, grid, block, 0, s, x, y, rows, cols);
   else if (nch <= 4)
-    cumsum_rows_reg<4, REV, VEC><<<grid, block, 0, s>>>(x, y, rows, cols);
+    ntl_launch_pdl(cumsum_rows_reg<4, REV, VEC>, grid, block, 0, s, x, y, rows, cols);
   else if (nch <= 8)
-    cumsum_rows_reg<8, REV, VEC><<<grid, block, 0, s>>>(x, y, rows, cols);
+    ntl_launch_pdl(cumsum_rows_reg<8, REV, VEC>, grid, block, 0, s, x, y, rows, cols);
   else
-    cumsum_rows_loop<REV, VEC><<<grid, block, 0, s>>>(x, y, rows, cols);
+    ntl_launch_pdl(cumsum_rows_loop<REV, VEC>, grid, block, 0, s, x, y, rows, cols);
   ntl_note_launch();
   return ntl_check_launch("cumsum launch");
 }

@@ -222,3 +222,81 @@ def test_native_launches_counted(torch_cuda):
     K.softmax(4, 64)(torch.randn(4, 64, device="cuda"))
     torch.cuda.synchronize()
     assert _lib.launch_count() == before + 1
+
+
+# ------------------------------------------------------------- back-to-back dependent launches
+#
+# The HBM-bound kernels are launched with programmatic stream serialization: the next kernel on
+# the stream may start while the previous one runs, and waits (griddepcontrol.wait) before its
+# first global access.  These tests chain kernels whose inputs are the previous kernel's output
+# (read after write) or whose outputs overwrite the previous kernel's input (write after read),
+# with no synchronisation in between, eagerly and inside a CUDA graph.
+
+
+def _ping_pong(torch, x, y, rows, cols, rounds, stream):
+    """Bit-exact ops only: y = cumsum(x); x = y - x (x is rewritten right after being read)."""
+    from ntilang_b200 import _lib
+
+    s = stream.cuda_stream
+    for _ in range(rounds):
+        _lib.call("ntl_cumsum_f32", x.data_ptr(), y.data_ptr(), rows, cols, 0, s)
+        _lib.call("ntl_binary_f32", 1, y.data_ptr(), x.data_ptr(), x.data_ptr(), rows * cols, s)
+
+
+def _four_ops(torch, x, y, w, rows, cols, stream):
+    """y = x + x; x = cumsum(y); y = softmax(x); x = rmsnorm(y, w): each reads the previous
+    output and overwrites a buffer the previous kernel read."""
+    from ntilang_b200 import _lib
+
+    s = stream.cuda_stream
+    _lib.call("ntl_vadd_f32", x.data_ptr(), x.data_ptr(), y.data_ptr(), rows * cols, s)
+    _lib.call("ntl_cumsum_f32", y.data_ptr(), x.data_ptr(), rows, cols, 0, s)
+    _lib.call("ntl_softmax_f32", x.data_ptr(), y.data_ptr(), rows, cols, s)
+    _lib.call("ntl_rmsnorm_f32", y.data_ptr(), w.data_ptr(), x.data_ptr(), rows, cols, 1e-6, 1.0 / cols, s)
+
+
+def _run(torch, graph, body):
+    stream = torch.cuda.Stream()
+    stream.wait_stream(torch.cuda.current_stream())
+    torch.cuda.synchronize()
+    if graph:
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            body(stream)
+        torch.cuda.synchronize()
+        with torch.cuda.stream(stream):
+            g.replay()
+    else:
+        body(stream)
+    torch.cuda.synchronize()
+
+
+@pytest.mark.parametrize("graph", [False, True])
+def test_dependent_launches_bit_exact_ping_pong(torch_cuda, graph):
+    torch = torch_cuda
+    rows, cols, rounds = 8192, 256, 4
+    x0 = np.random.default_rng(17).uniform(-1, 1, size=(rows, cols)).astype(np.float32)
+    expect = x0
+    for _ in range(rounds):
+        y = rowops.cumsum(expect)
+        expect = O.binary("-", y, expect)
+    x = to_gpu(torch, x0)
+    y = torch.empty_like(x)
+    _run(torch, graph, lambda st: _ping_pong(torch, x, y, rows, cols, rounds, st))
+    ok, bad = bits_equal(x.cpu().numpy(), expect)
+    assert ok, f"{bad} elements differ"
+
+
+@pytest.mark.parametrize("graph", [False, True])
+def test_dependent_launches_four_op_chain(torch_cuda, graph):
+    torch = torch_cuda
+    rows, cols = 8192, 256
+    rng = np.random.default_rng(18)
+    x0 = rng.uniform(-1, 1, size=(rows, cols)).astype(np.float32)
+    w0 = rng.normal(1.0, 0.1, size=cols).astype(np.float32)
+    expect = rowops.rmsnorm(rowops.softmax(rowops.cumsum(rowops.vadd(x0, x0))), w0, 1e-6)
+    x, w = to_gpu(torch, x0), to_gpu(torch, w0)
+    y = torch.empty_like(x)
+    _run(torch, graph, lambda st: _four_ops(torch, x, y, w, rows, cols, st))
+    # vadd and cumsum are bit-exact; softmax then RMSNorm each within 1e-5 of the oracle.
+    np.testing.assert_allclose(x.cpu().numpy(), expect, rtol=5e-5, atol=1e-7)
