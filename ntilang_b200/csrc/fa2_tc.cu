@@ -7,24 +7,25 @@
 // statistics (codegen.py:972-984, :1062-1073).
 //
 // Design: one CTA = one (batch, head, 256-query block) = two 128-row query tiles that
-// share every K/V tile (320 threads, 10 warps):
-//   warps 0-3   softmax, O rescale and the O / l -> fp16 epilogue of query tile 0, one row
-//               per thread (TMEM lane = row)
-//   warps 4-7   the same for query tile 1
-//   warp 8      TMEM owner (512 columns: S0, S1, O0, O1) and MMA issuer
-//   warp 9      TMA: Q0, Q1 once, then K_j (3-stage ring, released once both tiles' QK^T
-//               consumed it) and V_j (2-stage ring) with K running one tile ahead; 3-D
-//               tensor maps [B*H, S, D] zero-fill rows past S and never cross heads.
+// share every K/V tile (576 threads, 18 warps):
+//   warps 0-7   softmax, O rescale and the O / l -> fp16 epilogue of query tile 0: each warp
+//               owns 16 TMEM lanes (rows) x all 128 keys of S; through 16x256b accesses the
+//               four threads of a row sit in one warp (row max / sum by two shuffles)
+//   warps 8-15  the same for query tile 1
+//   warp 16     TMEM owner (512 columns: S0, S1, O0, O1) and MMA issuer
+//   warp 17     TMA: Q0, Q1 once, then K_j and V_j (2-stage rings each) with K running one
+//               tile ahead; 3-D tensor maps [B*H, S, D] zero-fill rows past S and never
+//               cross heads.
 // Per KV tile j the MMA warp issues, per query tile i: O_i += P_i V_j (A = P_i from TMEM,
-// fp16 packed in place over S_i; B = V_j N-major in smem) and then S_i = Q_i K_{j+1}^T
-// (both operands K-major in smem), so the tensor core works on one tile while the other
-// tile's softmax runs.  Softmax uses a lazily updated row max: O and l are rescaled only
-// when the max grows by more than 2^8 (P stays <= 256, exact in the final O / l).  S_i of
-// tile j is issued after P_i V_{j-1}, so once S_i is ready O_i is stable and the softmax
-// warps rescale it in place without another hand-off.  Masked scores (causal key > query, keys
-// >= S) contribute exactly 0, like the reference's -1e30 fill.  Every mbarrier wait is
-// bounded; a wait that gives up records a status code, drains in-flight copies and
-// MMAs, frees TMEM and returns.
+// fp16 pairs packed over the first 64 S_i columns; B = V_j N-major in smem) and then
+// S_i = Q_i K_{j+1}^T (both operands K-major in smem), so the tensor core works on one tile
+// while the other tile's softmax runs.  Softmax uses a lazily updated row max: O and l are
+// rescaled only when the max grows by more than 2^8 (P stays <= 256, exact in the final
+// O / l).  S_i of tile j is issued after P_i V_{j-1}, so once S_i is ready O_i is stable and
+// the softmax warps rescale it in place without another hand-off.  Masked scores (causal
+// key > query, keys >= S) contribute exactly 0, like the reference's -1e30 fill.  Every
+// mbarrier wait is bounded; a wait that gives up records a status code, drains in-flight
+// copies and MMAs, frees TMEM and returns.
 #include <atomic>
 #include <mutex>
 
@@ -59,11 +60,11 @@ struct __align__(16) Fa2Ctl {
   uint64_t s_full[QTILES];
   uint64_t sm_done[QTILES];
   uint64_t o_final[QTILES];
-  uint64_t pair[QTILES][4];  // the two half-row warps of (tile, lane quarter)
+  uint64_t l_ready[QTILES];  // the 8 softmax warps of a tile published their row sums
   uint64_t drain;
   uint32_t tmem_base;
   int abort;
-  float xmax[QTILES][2][BM];  // per-half row maxima, then per-half row sums
+  float lsum[QTILES][BM];    // row sums l, written once per tile at the end
 };
 
 template <int D>
@@ -117,6 +118,50 @@ __device__ __forceinline__ void exp2_fma2(uint64_t x2, float& p0, float& p1) {
   p1 = __uint_as_float(__float_as_uint(q1) + (__float_as_uint(t1) << 23));
 }
 
+// Scores of keys >= lim (per row) become -inf.  v is one 16x256b.x8 load: v[4g + e] holds key
+// key0 + 8g + (e&1) of row A (e < 2, limit limA) or row B (limit limB).
+__device__ __forceinline__ void mask_keys(uint32_t (&v)[32], int key0, int limA, int limB) {
+#pragma unroll
+  for (int g = 0; g < 8; ++g) {
+    const int key = key0 + 8 * g;
+    if (key >= limA) v[4 * g] = __float_as_uint(-INFINITY);
+    if (key + 1 >= limA) v[4 * g + 1] = __float_as_uint(-INFINITY);
+    if (key >= limB) v[4 * g + 2] = __float_as_uint(-INFINITY);
+    if (key + 1 >= limB) v[4 * g + 3] = __float_as_uint(-INFINITY);
+  }
+}
+
+// p = exp2(s*c - m*c) for one 16x256b.x8 block of scores (64 keys of rows A and B), row
+// sums into sA2 / sB2 (f32x2 partials), fp16 pairs of consecutive keys stored with a
+// 16x128b.x8 access at `p_addr` (32 packed columns).
+__device__ __forceinline__ void exp_pack_store(const uint32_t (&v)[32], uint64_t c2, uint64_t nA2, uint64_t nB2,
+                                               uint64_t (&sA2)[2], uint64_t (&sB2)[2], uint32_t p_addr) {
+  uint32_t pk[16];
+#pragma unroll
+  for (int g = 0; g < 8; ++g) {
+    const uint64_t xA = f2_fma(f2_make(__uint_as_float(v[4 * g]), __uint_as_float(v[4 * g + 1])), c2, nA2);
+    const uint64_t xB = f2_fma(f2_make(__uint_as_float(v[4 * g + 2]), __uint_as_float(v[4 * g + 3])), c2, nB2);
+    float a0, a1, b0, b1;
+    if ((g & 3) == 3) {  // a fixed quarter of the exponentials on the FMA pipe
+      exp2_fma2(xA, a0, a1);
+      exp2_fma2(xB, b0, b1);
+    } else {
+      float x0, x1;
+      f2_split(xA, x0, x1);
+      a0 = ex2_approx(x0);
+      a1 = ex2_approx(x1);
+      f2_split(xB, x0, x1);
+      b0 = ex2_approx(x0);
+      b1 = ex2_approx(x1);
+    }
+    sA2[g & 1] = f2_add(sA2[g & 1], f2_make(a0, a1));
+    sB2[g & 1] = f2_add(sB2[g & 1], f2_make(b0, b1));
+    pk[2 * g] = pack_half2(a0, a1);
+    pk[2 * g + 1] = pack_half2(b0, b1);
+  }
+  tmem_st_16x128b_x8(p_addr, pk);
+}
+
 // Number of KV tiles query tile i of block qb needs (0 when the tile is past S).
 __device__ __forceinline__ int kv_tiles(const Fa2Params& p, int q0_tile) {
   if (q0_tile >= p.S) return 0;
@@ -159,7 +204,7 @@ __global__ void __launch_bounds__(THREADS, 1) fa2_fwd_kernel(const __grid_consta
       mbar_init(&ctl->s_full[i], 1);
       mbar_init(&ctl->sm_done[i], SM_WARPS_PER_TILE);
       mbar_init(&ctl->o_final[i], 1);
-      for (int q = 0; q < 4; ++q) mbar_init(&ctl->pair[i][q], 2);
+      mbar_init(&ctl->l_ready[i], SM_WARPS_PER_TILE);
     }
     mbar_init(&ctl->drain, 1);
     ctl->abort = 0;
@@ -269,8 +314,8 @@ __global__ void __launch_bounds__(THREADS, 1) fa2_fwd_kernel(const __grid_consta
           tc_fence_after();
           const uint32_t v_addr = smem_u32(smem + L::V_OFF + s * L::KV_BYTES);
 #pragma unroll
-          for (int kk = 0; kk < BN / 16; ++kk)  // P_i: keys [64h, 64h+64) packed at S columns [64h, 64h+32)
-            tc_mma_f16_ts(tmem + L::O_COL(i), tmem + L::S_COL(i) + (kk >> 2) * 64 + (kk & 3) * 8,
+          for (int kk = 0; kk < BN / 16; ++kk)  // P_i: keys 2c, 2c+1 packed in S column c, c < 64
+            tc_mma_f16_ts(tmem + L::O_COL(i), tmem + L::S_COL(i) + kk * 8,
                           umma_desc_sw128(v_addr + kk * 2048, BN * 128, 1024), idesc_o, (j > 0 || kk > 0) ? 1u : 0u);
           if (j == n_t[i] - 1) tc_commit(&ctl->o_final[i]);
           if (j + 1 < n_t[i]) {
@@ -295,24 +340,30 @@ __global__ void __launch_bounds__(THREADS, 1) fa2_fwd_kernel(const __grid_consta
     }
   } else if (warp < 2 * SM_WARPS_PER_TILE) {
     // ------------------------------------------------------------------ softmax warps
-    // Warp w: query tile w/8, key half h = (w/4)&1 (keys [64h, 64h+64) of every KV tile and
-    // O columns [h*D/2, (h+1)*D/2)), TMEM lanes 32*(w&3)...: two threads per row.
+    // Warp w: query tile i = w/8, lane quarter q = w%4 (the TMEM lanes a warp may access) and
+    // sub-block sb = (w/4)%2: TMEM lanes 32q + 16sb .. +15, all BN keys.  Through 16x256b
+    // accesses thread t holds two rows (lanes +t/4 and +t/4+8) and, in each 8-key group, keys
+    // 2(t%4) and 2(t%4)+1; the four threads of a row are lanes t^1, t^2, t^3 of this warp, so
+    // row maxima and sums combine with two shuffles.  S stays in registers between the max
+    // and the exponentials; P (fp16 pairs of consecutive keys) is written back over the S
+    // columns this warp has already read.
     const int i = warp >> 3;
-    const int h = (warp >> 2) & 1;
     const int quarter = warp & 3;
-    const int r = quarter * 32 + lane;
+    const int sb = (warp >> 2) & 1;
+    const int lane_base = 32 * quarter + 16 * sb;
+    const int rA = lane_base + (lane >> 2), rB = rA + 8;  // this thread's rows of the tile
+    const int cq = 2 * (lane & 3);
     const int tile_q0 = q0 + i * BM;
-    const int qrow = tile_q0 + r;
-    const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
-    const uint32_t s_addr = tmem + lane_off + L::S_COL(i) + h * 64;  // this half's 64 S columns
-    const uint32_t o_addr = tmem + lane_off + L::O_COL(i) + h * (D / 2);
-    uint64_t* pair_bar = &ctl->pair[i][quarter];  // exchange barrier with the other half's warp
+    const uint32_t lane_off = static_cast<uint32_t>(lane_base) << 16;
+    const uint32_t s_addr = tmem + lane_off + L::S_COL(i);
+    const uint32_t o_addr = tmem + lane_off + L::O_COL(i);
     const float c = p.c;
-    const int key_lim = p.causal ? min(p.S, qrow + 1) : p.S;  // keys < key_lim are kept
-    float m_use = -INFINITY, l = 0.0f;  // l: this half's share of the row sum
+    const int limA = p.causal ? min(p.S, tile_q0 + rA + 1) : p.S;  // keys < lim are kept
+    const int limB = p.causal ? min(p.S, tile_q0 + rB + 1) : p.S;
+    float mA = -INFINITY, mB = -INFINITY;  // lazily updated row maxima
+    float lA = 0.0f, lB = 0.0f;            // this thread's share of the row sums
     bool ok = true;
     for (int j = 0; j < n_t[i]; ++j) {
-      const int k0 = j * BN + h * 64;  // first key of this half
       if (!mbar_wait_bounded(&ctl->s_full[i], j & 1, p.wait_limit, abort_flag)) {
         if (!*abort_flag) fa2_abort(ctl, NTL_STATUS_SOFTMAX_WAIT);
         ok = false;
@@ -320,121 +371,126 @@ __global__ void __launch_bounds__(THREADS, 1) fa2_fwd_kernel(const __grid_consta
       }
       __syncwarp();
       tc_fence_after();
+      // Low keys [0, 64) stay in registers from the max pass to the exponentials; the high
+      // keys are loaded again afterwards (their S columns are untouched until their own P
+      // store, which goes to packed columns [32, 64), i.e. low-key S columns already read).
+      uint32_t lo[32];  // lo[4g + e]: key 8g + cq + (e&1) of row A (e < 2) or row B
+      float mxA, mxB;
       const bool masked_tile = (j * BN + BN > p.S) || (p.causal && j * BN + BN - 1 > tile_q0);
-      // pass 1: max over this half, combined with the other half through shared memory
-      float hmax;
       {
-        uint32_t a[32], b[32];
-        tmem_ld_32x32b_x32(s_addr, a);
-        tmem_ld_32x32b_x32(s_addr + 32, b);
+        uint32_t hi[32];
+        tmem_ld_16x256b_x8(s_addr, lo);
+        tmem_ld_16x256b_x8(s_addr + 64, hi);
         tc_wait_ld();
-        float cm[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
         if (masked_tile) {
-#pragma unroll
-          for (int e = 0; e < 32; ++e) {
-            cm[e & 3] = fmaxf(cm[e & 3], k0 + e < key_lim ? __uint_as_float(a[e]) : -INFINITY);
-            cm[e & 3] = fmaxf(cm[e & 3], k0 + 32 + e < key_lim ? __uint_as_float(b[e]) : -INFINITY);
-          }
-        } else {
-#pragma unroll
-          for (int e = 0; e < 32; ++e) cm[e & 3] = fmax3(cm[e & 3], __uint_as_float(a[e]), __uint_as_float(b[e]));
+          mask_keys(lo, j * BN + cq, limA, limB);
+          mask_keys(hi, j * BN + 64 + cq, limA, limB);
         }
-        hmax = fmax3(fmaxf(cm[0], cm[1]), cm[2], cm[3]);
+        float xa0 = -INFINITY, xa1 = -INFINITY, xb0 = -INFINITY, xb1 = -INFINITY;
+#pragma unroll
+        for (int g = 0; g < 8; ++g) {
+          xa0 = fmax3(xa0, __uint_as_float(lo[4 * g]), __uint_as_float(lo[4 * g + 1]));
+          xb0 = fmax3(xb0, __uint_as_float(lo[4 * g + 2]), __uint_as_float(lo[4 * g + 3]));
+          xa1 = fmax3(xa1, __uint_as_float(hi[4 * g]), __uint_as_float(hi[4 * g + 1]));
+          xb1 = fmax3(xb1, __uint_as_float(hi[4 * g + 2]), __uint_as_float(hi[4 * g + 3]));
+        }
+        mxA = fmaxf(xa0, xa1);
+        mxB = fmaxf(xb0, xb1);
       }
-      ctl->xmax[i][h][r] = hmax;
-      __syncwarp();
-      if (lane == 0) mbar_arrive(pair_bar);
-      if (!mbar_wait_bounded(pair_bar, j & 1, p.wait_limit, abort_flag)) {
-        if (!*abort_flag) fa2_abort(ctl, NTL_STATUS_SOFTMAX_WAIT);
-        ok = false;
-        break;
-      }
-      const float mx = fmaxf(hmax, ctl->xmax[i][h ^ 1][r]);
-      // lazy max (both halves take the same decision from the same values)
-      float rs = 1.0f;
+      mxA = fmaxf(mxA, __shfl_xor_sync(0xffffffffu, mxA, 1));
+      mxB = fmaxf(mxB, __shfl_xor_sync(0xffffffffu, mxB, 1));
+      mxA = fmaxf(mxA, __shfl_xor_sync(0xffffffffu, mxA, 2));
+      mxB = fmaxf(mxB, __shfl_xor_sync(0xffffffffu, mxB, 2));
+      // lazy max: the four threads of a row take the same decision from the same values
+      float rsA = 1.0f, rsB = 1.0f;
       bool moved = false;
       if (j == 0) {
-        m_use = mx;
-      } else if ((mx - m_use) * c > kRescaleLog2) {
-        rs = ex2_approx((m_use - mx) * c);
-        m_use = mx;
-        moved = true;
+        mA = mxA;
+        mB = mxB;
+      } else {
+        if ((mxA - mA) * c > kRescaleLog2) {
+          rsA = ex2_approx((mA - mxA) * c);
+          mA = mxA;
+          moved = true;
+        }
+        if ((mxB - mB) * c > kRescaleLog2) {
+          rsB = ex2_approx((mB - mxB) * c);
+          mB = mxB;
+          moved = true;
+        }
       }
       if (__any_sync(0xffffffffu, moved)) {
         // O_i = P_{<j} V is complete: S_i of this tile was issued after the last P_i V.
 #pragma unroll 1
-        for (int ch = 0; ch < D / 32; ++ch) {
-          uint32_t o[16];
-          tmem_ld_32x32b_x16(o_addr + ch * 16, o);
+        for (int ch = 0; ch < D / 64; ++ch) {
+          uint32_t o[32];
+          tmem_ld_16x256b_x8(o_addr + ch * 64, o);
           tc_wait_ld();
 #pragma unroll
-          for (int e = 0; e < 16; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * rs);
-          tmem_st_32x32b_x16(o_addr + ch * 16, o);
-        }
-      }
-      // pass 2: p = exp2(s*c - m*c) -> fp16 P packed over this half's own S columns
-      const float mc = m_use * c;
-      const uint64_t c2 = f2_make(c, c), nmc2 = f2_make(-mc, -mc);
-      uint64_t acc2[4] = {0ull, 0ull, 0ull, 0ull};
-#pragma unroll 1
-      for (int ch = 0; ch < 2; ++ch) {
-        uint32_t v[32];
-        tmem_ld_32x32b_x32(s_addr + ch * 32, v);
-        tc_wait_ld();
-        if (masked_tile) {
-#pragma unroll
-          for (int e = 0; e < 32; ++e)
-            if (k0 + ch * 32 + e >= key_lim) v[e] = __float_as_uint(-INFINITY);
-        }
-        uint32_t pk[16];
-#pragma unroll
-        for (int e = 0; e < 16; ++e) {
-          const uint64_t x2 = f2_fma(f2_make(__uint_as_float(v[2 * e]), __uint_as_float(v[2 * e + 1])), c2, nmc2);
-          float p0, p1;
-          if ((e & 3) == 3) {  // a fixed quarter of the pairs on the FMA pipe
-            exp2_fma2(x2, p0, p1);
-          } else {
-            float x0, x1;
-            f2_split(x2, x0, x1);
-            p0 = ex2_approx(x0);
-            p1 = ex2_approx(x1);
+          for (int g = 0; g < 8; ++g) {
+            o[4 * g] = __float_as_uint(__uint_as_float(o[4 * g]) * rsA);
+            o[4 * g + 1] = __float_as_uint(__uint_as_float(o[4 * g + 1]) * rsA);
+            o[4 * g + 2] = __float_as_uint(__uint_as_float(o[4 * g + 2]) * rsB);
+            o[4 * g + 3] = __float_as_uint(__uint_as_float(o[4 * g + 3]) * rsB);
           }
-          acc2[e & 3] = f2_add(acc2[e & 3], f2_make(p0, p1));
-          pk[e] = pack_half2(p0, p1);
+          tmem_st_16x256b_x8(o_addr + ch * 64, o);
         }
-        // keys [k0 + 32ch, +32) -> packed columns [16ch, 16ch + 16) of this half (already read)
-        tmem_st_32x32b_x16(s_addr + ch * 16, pk);
       }
-      float sum;
+      // p = exp2(s*c - m*c) -> fp16 pairs; keys [64hf, 64hf + 64) -> packed columns [32hf, 32hf + 32)
+      const uint64_t c2 = f2_make(c, c);
+      const uint64_t nA2 = f2_make(-mA * c, -mA * c), nB2 = f2_make(-mB * c, -mB * c);
+      uint64_t sA2[2] = {0ull, 0ull}, sB2[2] = {0ull, 0ull};
+      exp_pack_store(lo, c2, nA2, nB2, sA2, sB2, s_addr);
       {
-        float a0, a1;
-        f2_split(f2_add(f2_add(acc2[0], acc2[1]), f2_add(acc2[2], acc2[3])), a0, a1);
-        sum = a0 + a1;
+        uint32_t hi[32];
+        tmem_ld_16x256b_x8(s_addr + 64, hi);
+        tc_wait_ld();
+        if (masked_tile) mask_keys(hi, j * BN + 64 + cq, limA, limB);
+        exp_pack_store(hi, c2, nA2, nB2, sA2, sB2, s_addr + 32);
       }
-      l = (j == 0) ? sum : __fmaf_rn(l, rs, sum);
+      float sumA, sumB;
+      {
+        float u0, u1;
+        f2_split(f2_add(sA2[0], sA2[1]), u0, u1);
+        sumA = u0 + u1;
+        f2_split(f2_add(sB2[0], sB2[1]), u0, u1);
+        sumB = u0 + u1;
+      }
+      lA = (j == 0) ? sumA : __fmaf_rn(lA, rsA, sumA);
+      lB = (j == 0) ? sumB : __fmaf_rn(lB, rsB, sumB);
       tc_wait_st();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&ctl->sm_done[i]);
     }
-    // epilogue: O / (l_0 + l_1) -> fp16, each half its D/2 columns
+    // epilogue: row sums to shared memory, then O / l -> fp16 with 32x32b accesses (thread =
+    // row 32q + lane, columns [sb*D/2, sb*D/2 + D/2)).
     if (ok && n_t[i] > 0) {
-      ctl->xmax[i][h][r] = l;
+      lA += __shfl_xor_sync(0xffffffffu, lA, 1);
+      lB += __shfl_xor_sync(0xffffffffu, lB, 1);
+      lA += __shfl_xor_sync(0xffffffffu, lA, 2);
+      lB += __shfl_xor_sync(0xffffffffu, lB, 2);
+      if ((lane & 3) == 0) {
+        ctl->lsum[i][rA] = lA;
+        ctl->lsum[i][rB] = lB;
+      }
       __syncwarp();
-      if (lane == 0) mbar_arrive(pair_bar);
-      const bool paired = mbar_wait_bounded(pair_bar, n_t[i] & 1, p.wait_limit, abort_flag);
-      const float l_row = l + ctl->xmax[i][h ^ 1][r];
-      if (!paired || !mbar_wait_bounded(&ctl->o_final[i], 0, p.wait_limit, abort_flag)) {
+      if (lane == 0) mbar_arrive(&ctl->l_ready[i]);
+      const int r = quarter * 32 + lane;
+      const int qrow = tile_q0 + r;
+      const uint32_t o_row = tmem + (static_cast<uint32_t>(quarter * 32) << 16) + L::O_COL(i) + sb * (D / 2);
+      if (!mbar_wait_bounded(&ctl->l_ready[i], 0, p.wait_limit, abort_flag) ||
+          !mbar_wait_bounded(&ctl->o_final[i], 0, p.wait_limit, abort_flag)) {
         if (!*abort_flag) fa2_abort(ctl, NTL_STATUS_SOFTMAX_WAIT);
       } else {
         __syncwarp();
         tc_fence_after();
-        const float inv_l = 1.0f / l_row;
-        __half* orow = p.o + (static_cast<int64_t>(bh) * p.S + qrow) * D + h * (D / 2);
+        const float inv_l = 1.0f / ctl->lsum[i][r];
+        __half* orow = p.o + (static_cast<int64_t>(bh) * p.S + qrow) * D + sb * (D / 2);
 #pragma unroll 1
         for (int ch = 0; ch < D / 32; ++ch) {
           uint32_t o[16];
-          tmem_ld_32x32b_x16(o_addr + ch * 16, o);
+          tmem_ld_32x32b_x16(o_row + ch * 16, o);
           tc_wait_ld();
           if (qrow < p.S) {
             uint32_t hv[8];
