@@ -19,7 +19,10 @@
 // Per KV tile j the MMA warp issues, per query tile i: O_i += P_i V_j (A = P_i from TMEM,
 // fp16 pairs packed over the first 64 S_i columns; B = V_j N-major in smem) and then
 // S_i = Q_i K_{j+1}^T (both operands K-major in smem), so the tensor core works on one tile
-// while the other tile's softmax runs.  Softmax uses a lazily updated row max: O and l are
+// while the other tile's softmax runs.  The softmax warps signal the low-key half of P as
+// soon as it is in TMEM, and the MMA warp starts P V on those keys while the high half is
+// computed; the MMA warp checks V_j and K_{j+1} before it waits for the softmax, and spins
+// (bounded, never suspended) on the softmax hand-offs.  Softmax uses a lazily updated row max: O and l are
 // rescaled only when the max grows by more than 2^8 (P stays <= 256, exact in the final
 // O / l).  S_i of tile j is issued after P_i V_{j-1}, so once S_i is ready O_i is stable and
 // the softmax warps rescale it in place without another hand-off.  Masked scores (causal
@@ -59,6 +62,7 @@ struct __align__(16) Fa2Ctl {
   uint64_t k_full[KSTAGES], k_empty[KSTAGES], v_full[VSTAGES], v_empty[VSTAGES];
   uint64_t s_full[QTILES];
   uint64_t sm_done[QTILES];
+  uint64_t p_lo[QTILES];     // the low-key half of P_i is in TMEM (8 warps)
   uint64_t o_final[QTILES];
   uint64_t l_ready[QTILES];  // the 8 softmax warps of a tile published their row sums
   uint64_t drain;
@@ -162,6 +166,7 @@ __device__ __forceinline__ void exp_pack_store(const uint32_t (&v)[32], uint64_t
   tmem_st_16x128b_x8(p_addr, pk);
 }
 
+
 // Number of KV tiles query tile i of block qb needs (0 when the tile is past S).
 __device__ __forceinline__ int kv_tiles(const Fa2Params& p, int q0_tile) {
   if (q0_tile >= p.S) return 0;
@@ -203,6 +208,7 @@ __global__ void __launch_bounds__(THREADS, 1) fa2_fwd_kernel(const __grid_consta
     for (int i = 0; i < QTILES; ++i) {
       mbar_init(&ctl->s_full[i], 1);
       mbar_init(&ctl->sm_done[i], SM_WARPS_PER_TILE);
+      mbar_init(&ctl->p_lo[i], SM_WARPS_PER_TILE);
       mbar_init(&ctl->o_final[i], 1);
       mbar_init(&ctl->l_ready[i], SM_WARPS_PER_TILE);
     }
@@ -279,6 +285,11 @@ __global__ void __launch_bounds__(THREADS, 1) fa2_fwd_kernel(const __grid_consta
       constexpr uint32_t idesc_o = umma_idesc_f16_f32(BM, D, 0, 1);   // B = V tile, N-major
       bool ok = mbar_wait_bounded(&ctl->q_full, 0, p.wait_limit, abort_flag);
       if (!ok && !*abort_flag) fa2_abort(ctl, NTL_STATUS_MMA_FULL_WAIT);
+      auto spin_or_abort = [&](uint64_t* bar, uint32_t parity) -> bool {
+        if (mbar_spin_bounded(bar, parity, p.wait_limit, abort_flag)) return true;
+        if (!*abort_flag) fa2_abort(ctl, NTL_STATUS_MMA_FULL_WAIT);
+        return false;
+      };
       auto wait_or_abort = [&](uint64_t* bar, uint32_t parity) -> bool {
         if (mbar_wait_bounded(bar, parity, p.wait_limit, abort_flag)) return true;
         if (!*abort_flag) fa2_abort(ctl, NTL_STATUS_MMA_FULL_WAIT);
@@ -307,25 +318,37 @@ __global__ void __launch_bounds__(THREADS, 1) fa2_fwd_kernel(const __grid_consta
         const int s = j % VSTAGES;
         for (int i = 0; i < QTILES && ok; ++i) {
           if (j >= n_t[i]) continue;
-          if (!wait_or_abort(&ctl->sm_done[i], j & 1) || !wait_or_abort(&ctl->v_full[s], (j / VSTAGES) & 1)) {
+          // V_j and K_{j+1} were loaded long before the softmax finishes: check them first,
+          // so that only the softmax hand-off is on the critical path.
+          if (!wait_or_abort(&ctl->v_full[s], (j / VSTAGES) & 1)) {
+            ok = false;
+            break;
+          }
+          if (j + 1 < n_t[i] && !wait_or_abort(&ctl->k_full[(j + 1) % KSTAGES], ((j + 1) / KSTAGES) & 1)) {
+            ok = false;
+            break;
+          }
+          if (!spin_or_abort(&ctl->p_lo[i], j & 1)) {
             ok = false;
             break;
           }
           tc_fence_after();
           const uint32_t v_addr = smem_u32(smem + L::V_OFF + s * L::KV_BYTES);
 #pragma unroll
-          for (int kk = 0; kk < BN / 16; ++kk)  // P_i: keys 2c, 2c+1 packed in S column c, c < 64
+          for (int kk = 0; kk < BN / 32; ++kk)  // keys [0, 64): packed S columns [0, 32)
             tc_mma_f16_ts(tmem + L::O_COL(i), tmem + L::S_COL(i) + kk * 8,
                           umma_desc_sw128(v_addr + kk * 2048, BN * 128, 1024), idesc_o, (j > 0 || kk > 0) ? 1u : 0u);
-          if (j == n_t[i] - 1) tc_commit(&ctl->o_final[i]);
-          if (j + 1 < n_t[i]) {
-            if (!wait_or_abort(&ctl->k_full[(j + 1) % KSTAGES], ((j + 1) / KSTAGES) & 1)) {
-              ok = false;
-              break;
-            }
-            tc_fence_after();
-            issue_s(i, j + 1);
+          if (!spin_or_abort(&ctl->sm_done[i], j & 1)) {
+            ok = false;
+            break;
           }
+          tc_fence_after();
+#pragma unroll
+          for (int kk = BN / 32; kk < BN / 16; ++kk)  // keys [64, 128): packed S columns [32, 64)
+            tc_mma_f16_ts(tmem + L::O_COL(i), tmem + L::S_COL(i) + kk * 8,
+                          umma_desc_sw128(v_addr + kk * 2048, BN * 128, 1024), idesc_o, 1u);
+          if (j == n_t[i] - 1) tc_commit(&ctl->o_final[i]);
+          if (j + 1 < n_t[i]) issue_s(i, j + 1);
         }
         if (ok) {
           tc_commit(&ctl->v_empty[s]);                                    // V_j consumed by both P V
@@ -440,10 +463,14 @@ __global__ void __launch_bounds__(THREADS, 1) fa2_fwd_kernel(const __grid_consta
       const uint64_t c2 = f2_make(c, c);
       const uint64_t nA2 = f2_make(-mA * c, -mA * c), nB2 = f2_make(-mB * c, -mB * c);
       uint64_t sA2[2] = {0ull, 0ull}, sB2[2] = {0ull, 0ull};
-      exp_pack_store(lo, c2, nA2, nB2, sA2, sB2, s_addr);
       {
         uint32_t hi[32];
         tmem_ld_16x256b_x8(s_addr + 64, hi);
+        exp_pack_store(lo, c2, nA2, nB2, sA2, sB2, s_addr);
+        tc_wait_st();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&ctl->p_lo[i]);
         tc_wait_ld();
         if (masked_tile) mask_keys(hi, j * BN + 64 + cq, limA, limB);
         exp_pack_store(hi, c2, nA2, nB2, sA2, sB2, s_addr + 32);

@@ -146,6 +146,21 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
   return false;
 }
 
+// Bounded wait that never suspends the thread: non-blocking probes only (for a thread whose
+// only job is to react to this barrier quickly).
+__device__ __forceinline__ bool mbar_spin_bounded(uint64_t* bar, uint32_t parity, int64_t limit,
+                                                  volatile int* abort_flag) {
+  const uint64_t t0 = global_ns();
+  for (int64_t i = 0; i < limit; ++i) {
+    if (mbar_test_wait(bar, parity)) return true;
+    if ((i & 255) == 255) {
+      if (abort_flag != nullptr && *abort_flag) return false;
+      if (global_ns() - t0 > kWaitCapNs) return false;
+    }
+  }
+  return false;
+}
+
 // ---- TMA (no multicast)
 __device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* map, uint64_t* bar, int32_t x,
                                             int32_t y) {
