@@ -95,17 +95,19 @@ int ntl_gemm_f16_f32(const uint16_t* a, const uint16_t* b, float* c, const float
 int ntl_gemm_workspace_size(int64_t M, int64_t N, int64_t K, int b_trans, uint64_t* bytes_out);
 
 /* ntl_gemm_f16_f32 with a caller-owned workspace of at least ntl_gemm_workspace_size bytes
- * (16-byte aligned, zero-filled before its first use; every successful call leaves its flag
- * words zero again).  The last, partial wave of output tiles is split along K over all SMs
- * (stream-K) and reduced through the workspace.  Calls sharing a workspace must not overlap
- * on the GPU.  Replaces the same FFI call as ntl_gemm_f16_f32 (codegen.py:969-1026). */
+ * (16-byte aligned).  Its first 4 KB hold flag words that must be zero before the first use;
+ * every successful call leaves them zero again, whatever the shape, so one workspace serves
+ * every shape that fits it.  The last, partial wave of output tiles is split along K and
+ * reduced through the workspace: over all SMs (stream-K) for M <= 128, into 2-4 pieces on
+ * idle CTA pairs for M > 128.  Calls sharing a workspace must not overlap on the GPU.
+ * Replaces the same FFI call as ntl_gemm_f16_f32 (codegen.py:969-1026). */
 int ntl_gemm_f16_f32_ws(const uint16_t* a, const uint16_t* b, float* c, const float* bias, int bias_mode,
                         float alpha, int relu, int64_t M, int64_t N, int64_t K, int b_trans, void* workspace,
                         uint64_t workspace_bytes, ntl_stream_t stream);
 
 /* ntl_gemm_f16_f32_ws for callers that cannot allocate device memory (e.g. a plugin host
  * that passes only tensors and a stream, or a runtime with the device allocator switched
- * off): the stream-K scratch lives in a 16 MiB file-scope device array that every GPU
+ * off): the split-K scratch lives in a 16 MiB file-scope device array that every GPU
  * loading the library holds until exit.  Shapes whose plan needs more scratch than that
  * return NTL_ERR_UNSUPPORTED.  The first call on a device looks up the array's device
  * address (cudaGetSymbolAddress) and should come before any stream capture.  Calls share

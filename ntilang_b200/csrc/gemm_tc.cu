@@ -15,8 +15,9 @@
 //               tile i overlap the main loop of tile i+1.
 // Work schedule: whole waves of output tiles are data-parallel (one CTA computes a tile over
 // all of K).  With a workspace (ntl_gemm_f16_f32_ws), the tiles of the last, partial wave
-// are split along K evenly over all CTAs (stream-K): a CTA that starts a tile mid-K writes
-// its fp32 partial sum to its workspace slot and raises its flag; the CTA holding the
+// are split along K: here (M <= 128) evenly over all CTAs (stream-K), in the CTA-pair kernel
+// below (M > 128) into 2-4 equal pieces on otherwise idle pairs.  A CTA whose range starts
+// mid-K writes its fp32 partial sum to a workspace slot and raises a flag; the CTA holding the
 // tile's first k-block waits for those flags (bounded), adds the partials and runs the
 // epilogue.  Without a workspace every tile is data-parallel.
 // Every mbarrier / flag wait is bounded (ntl_set_wait_limit and a 2 s wall-clock cap); a
@@ -37,10 +38,17 @@ constexpr int B_STAGE = BN * BK * 2;        // 32 KB
 constexpr int STAGE_BYTES = A_STAGE + B_STAGE;
 constexpr int THREADS = 192;
 constexpr int TMEM_COLS = 512;
-constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*barriers*/ + 1024 /*alignment slack*/;
+// Per epilogue warp, the bias values of the current tile's BN columns (bias[N] form).
+constexpr int BIAS_SMEM_BYTES = 4 * BN * 4;
+constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*barriers*/ + BIAS_SMEM_BYTES + 1024 /*alignment slack*/;
 constexpr int GROUP_M = 8;
 constexpr int SK_MIN_UNITS = 8;             // fewest k-blocks a stream-K CTA takes
 constexpr size_t SK_SLOT_FLOATS = size_t(BM) * BN;
+// Workspace layout shared by every plan: a fixed block of flag words first (so that the
+// flags of one shape never land on another shape's partial sums when a workspace is reused),
+// then the partial-sum slots of SK_SLOT_FLOATS floats each.
+constexpr size_t kWsFlagBytes = 4096;
+constexpr size_t kWsMaxSlots = kWsFlagBytes / 4;
 
 __device__ uint32_t g_gemm_status;
 
@@ -53,6 +61,7 @@ struct GemmParams {
   int M, N, K;
   int b_trans;
   int vec_store;  // C rows 16-byte aligned
+  int vec_bias;   // bias 16-byte aligned and N % 4 == 0
   int64_t wait_limit;
   // work plan
   int num_m, num_n, kb;  // tile grid and k-blocks per tile
@@ -135,17 +144,52 @@ __device__ __forceinline__ float epi(float acc, float alpha, float b, int relu, 
   return relu ? fmaxf(v, 0.0f) : v;
 }
 
+// bias[n0 .. n0 + BN) (zero past N) -> this warp's shared-memory copy, read back by broadcast
+// in store_row_chunk.  One pass of 128-bit loads per tile instead of one load per output.
+__device__ __forceinline__ void stage_bias_n(const GemmParams& p, int n0, float* bias_s, int lane) {
+#pragma unroll
+  for (int c = lane * 4; c < BN; c += 128) {
+    const int col = n0 + c;
+    float4 t;
+    if (p.vec_bias && col + 3 < p.N) {
+      t = __ldg(reinterpret_cast<const float4*>(p.bias + col));
+    } else {
+      t.x = col < p.N ? __ldg(p.bias + col) : 0.0f;
+      t.y = col + 1 < p.N ? __ldg(p.bias + col + 1) : 0.0f;
+      t.z = col + 2 < p.N ? __ldg(p.bias + col + 2) : 0.0f;
+      t.w = col + 3 < p.N ? __ldg(p.bias + col + 3) : 0.0f;
+    }
+    *reinterpret_cast<float4*>(bias_s + c) = t;
+  }
+  __syncwarp();
+}
+
 // Epilogue of 32 accumulator columns [col0, col0+32) of one output row: alpha, bias, ReLU,
 // then 128-bit stores when the row is 16-byte aligned and the chunk lies inside C.
+// bias_chunk: the chunk's 32 bias[N] values in shared memory (bias[N] form only).
 __device__ __forceinline__ void store_row_chunk(float (&v)[32], const GemmParams& p, int row, int col0, float* crow,
-                                                float row_bias) {
+                                                float row_bias, const float* bias_chunk) {
+  if (p.bias_mode == NTL_BIAS_MN && p.vec_bias && col0 + 32 <= p.N) {
+    const float4* brow = reinterpret_cast<const float4*>(p.bias + static_cast<int64_t>(row) * p.N + col0);
+    float4 b4[8];
 #pragma unroll
-  for (int j = 0; j < 32; ++j) {
-    float b = row_bias;
-    const int col = col0 + j;
-    if (p.bias_mode == NTL_BIAS_N) b = (col < p.N) ? __ldg(p.bias + col) : 0.0f;
-    else if (p.bias_mode == NTL_BIAS_MN) b = (col < p.N) ? __ldg(p.bias + static_cast<int64_t>(row) * p.N + col) : 0.0f;
-    v[j] = epi(v[j], p.alpha, b, p.relu, p.bias_mode);
+    for (int q = 0; q < 8; ++q) b4[q] = __ldg(brow + q);
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      v[4 * q] = epi(v[4 * q], p.alpha, b4[q].x, p.relu, 1);
+      v[4 * q + 1] = epi(v[4 * q + 1], p.alpha, b4[q].y, p.relu, 1);
+      v[4 * q + 2] = epi(v[4 * q + 2], p.alpha, b4[q].z, p.relu, 1);
+      v[4 * q + 3] = epi(v[4 * q + 3], p.alpha, b4[q].w, p.relu, 1);
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      float b = row_bias;
+      const int col = col0 + j;
+      if (p.bias_mode == NTL_BIAS_N) b = bias_chunk[j];
+      else if (p.bias_mode == NTL_BIAS_MN) b = (col < p.N) ? __ldg(p.bias + static_cast<int64_t>(row) * p.N + col) : 0.0f;
+      v[j] = epi(v[j], p.alpha, b, p.relu, p.bias_mode);
+    }
   }
   if (p.vec_store && col0 + 32 <= p.N) {
 #pragma unroll
@@ -386,6 +430,8 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_tc_kernel(const __grid_consta
       const bool row_ok = row < p.M;
       float* crow = p.c + static_cast<int64_t>(row) * p.N;
       const float row_bias = (p.bias_mode == NTL_BIAS_M && row_ok) ? __ldg(p.bias + row) : 0.0f;
+      float* bias_s = reinterpret_cast<float*>(smem + STAGES * STAGE_BYTES + 1024) + (warp - 2) * BN;
+      if (p.bias_mode == NTL_BIAS_N) stage_bias_n(p, nb * BN, bias_s, lane);
       for (int chunk = 0; chunk < BN / 32; ++chunk) {
         uint32_t r[32];
         tmem_ld_32x32b_x32(t_row + chunk * 32, r);
@@ -403,7 +449,7 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_tc_kernel(const __grid_consta
         }
         const int col0 = nb * BN + chunk * 32;
         if (!row_ok || col0 >= p.N) continue;
-        store_row_chunk(v, p, row, col0, crow, row_bias);
+        store_row_chunk(v, p, row, col0, crow, row_bias, bias_s + chunk * 32);
       }
       tc_fence_before();
       __syncwarp();
@@ -441,6 +487,9 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_tc_kernel(const __grid_consta
 //                       CTAs (commit multicast, no multicast loads).
 //   warps 2..5          epilogue of the CTA's 128 rows; they free an accumulator by
 //                       arriving on the even CTA's `acc_empty` (8 arrivals).
+// With a workspace, the last partial wave's tiles are split along K (PairIter); a split
+// tile's piece 0 adds the other pieces' partial sums (workspace slots behind bounded flag
+// waits) before its epilogue.
 // Teardown: both CTAs meet at a cluster barrier; if any role gave up, the even CTA's
 // producer balances and waits out every stage load either CTA still has in flight (it knows
 // both issue counts), then both meet again before TMEM is freed.
@@ -451,7 +500,7 @@ constexpr int PR_STAGES = 6;
 constexpr int PR_A_STAGE = PR_BM * BK * 2;       // 16 KB
 constexpr int PR_B_STAGE = PR_BN_HALF * BK * 2;  // 16 KB
 constexpr int PR_STAGE_BYTES = PR_A_STAGE + PR_B_STAGE;
-constexpr int PR_SMEM_BYTES = PR_STAGES * PR_STAGE_BYTES + 1024 + 1024;
+constexpr int PR_SMEM_BYTES = PR_STAGES * PR_STAGE_BYTES + 1024 + BIAS_SMEM_BYTES + 1024;
 static_assert(PR_SMEM_BYTES <= 227 * 1024, "pair kernel shared memory");
 
 struct __align__(8) PairCtl {
@@ -460,10 +509,51 @@ struct __align__(8) PairCtl {
   uint64_t acc_full[2];       // each CTA: accumulator complete
   uint64_t acc_empty[2];      // rank 0: the 8 epilogue warps of the pair drained it
   uint64_t drain;
+  uint64_t sk_stored;         // each CTA: its 4 epilogue warps wrote a partial sum
+  uint64_t sk_read;           // each CTA: its 4 epilogue warps read every contributor flag
   uint32_t tmem_base;
   int abort;
   int issued;       // rank 0: stage loads its producer issued
   int peer_issued;  // rank 0: stage loads the odd CTA's producer issued
+};
+
+// Work of one pair: its data-parallel tiles (tile = pair + i * pairs < dp_tiles), then at most
+// one K-piece of a split tile.  The last partial wave's tiles (dp_tiles .. tiles) are each split
+// into `split` = p.sk_units K-ranges over p.sk_ctas = (tiles - dp_tiles) * split pairs; in each
+// group of `split` consecutive pairs the highest one holds piece 0 (k-blocks from 0) and
+// finalises the tile, so every pair it waits for was launched before it.
+struct PairWork {
+  int tile, k0, k1;
+  int piece;  // 0: data-parallel or finaliser; > 0: contributor
+  int slot;   // first workspace slot of this tile's contributors (split tiles only)
+};
+
+struct PairIter {
+  int t;
+  bool split_left;
+  __device__ __forceinline__ void init(const GemmParams& p, int pair) {
+    t = pair;
+    split_left = pair < p.sk_ctas;
+  }
+  __device__ __forceinline__ bool next(const GemmParams& p, int pair, int num_pairs, PairWork& w) {
+    if (t < p.dp_tiles) {
+      w.tile = t, w.k0 = 0, w.k1 = p.kb, w.piece = 0, w.slot = 0;
+      t += num_pairs;
+      return true;
+    }
+    if (split_left) {
+      split_left = false;
+      const int split = static_cast<int>(p.sk_units);
+      const int tl = pair / split;
+      w.piece = (split - 1) - pair % split;
+      w.tile = p.dp_tiles + tl;
+      w.k0 = static_cast<int>(static_cast<int64_t>(p.kb) * w.piece / split);
+      w.k1 = static_cast<int>(static_cast<int64_t>(p.kb) * (w.piece + 1) / split);
+      w.slot = tl * (split - 1);
+      return true;
+    }
+    return false;
+  }
 };
 
 __device__ __forceinline__ void pair_abort(PairCtl* ctl, uint32_t code) {
@@ -487,7 +577,6 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_pair_kernel(const __grid_cons
   const uint32_t rank = cluster_ctarank();
   const int pair = blockIdx.x >> 1;
   const int num_pairs = gridDim.x >> 1;
-  const int tiles = p.num_m * p.num_n;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < PR_STAGES; ++s) {
@@ -499,6 +588,8 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_pair_kernel(const __grid_cons
       mbar_init(&ctl->acc_empty[a], 8);
     }
     mbar_init(&ctl->drain, 1);
+    mbar_init(&ctl->sk_stored, 4);
+    mbar_init(&ctl->sk_read, 4);
     ctl->abort = 0;
     ctl->issued = 0;
     ctl->peer_issued = 0;
@@ -522,13 +613,16 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_pair_kernel(const __grid_cons
       int stage = 0;
       uint32_t phase = 0;
       int issued = 0;
-      for (int t = pair; t < tiles; t += num_pairs) {
+      PairIter it;
+      it.init(p, pair);
+      PairWork w;
+      while (it.next(p, pair, num_pairs, w)) {
         int mb, nb;
-        tile_coords(t, p.num_m, p.num_n, mb, nb);
+        tile_coords(w.tile, p.num_m, p.num_n, mb, nb);
         const int m0 = mb * PR_TILE_M + static_cast<int>(rank) * PR_BM;
         const int n0 = nb * BN + static_cast<int>(rank) * PR_BN_HALF;
         bool ok = true;
-        for (int kb = 0; kb < p.kb; ++kb) {
+        for (int kb = w.k0; kb < w.k1; ++kb) {
           if (!mbar_wait_bounded(&ctl->empty[stage], phase ^ 1, p.wait_limit, abort_flag)) {
             if (!*abort_flag) pair_abort(ctl, NTL_STATUS_TMA_EMPTY_WAIT);
             ok = false;
@@ -562,7 +656,10 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_pair_kernel(const __grid_cons
       uint32_t phase = 0;
       bool ok = true;
       int local = 0;
-      for (int t = pair; ok && t < tiles; t += num_pairs, ++local) {
+      PairIter it;
+      it.init(p, pair);
+      PairWork w;
+      for (; ok && it.next(p, pair, num_pairs, w); ++local) {
         const int acc = local & 1;
         const uint32_t acc_phase = (local >> 1) & 1;
         if (!mbar_wait_bounded(&ctl->acc_empty[acc], acc_phase ^ 1, p.wait_limit, abort_flag)) {
@@ -571,7 +668,7 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_pair_kernel(const __grid_cons
         }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * BN;
-        for (int kb = 0; kb < p.kb; ++kb) {
+        for (int kb = w.k0; kb < w.k1; ++kb) {
           if (!mbar_wait_bounded(&ctl->full[stage], phase, p.wait_limit, abort_flag)) {
             if (!*abort_flag) pair_abort(ctl, NTL_STATUS_MMA_FULL_WAIT);
             ok = false;
@@ -585,7 +682,7 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_pair_kernel(const __grid_cons
             const uint64_t adesc = umma_desc_sw128(a_addr + k * 32, 16, 1024);
             const uint64_t bdesc = p.b_trans ? umma_desc_sw128(b_addr + k * 32, 16, 1024)
                                              : umma_desc_sw128(b_addr + k * 2048, 64 * BK * 2, 1024);
-            tc_mma_f16_ss_pair(d_tmem, adesc, bdesc, idesc, (kb > 0 || k > 0) ? 1u : 0u);
+            tc_mma_f16_ss_pair(d_tmem, adesc, bdesc, idesc, (kb > w.k0 || k > 0) ? 1u : 0u);
           }
           tc_commit_pair_mc(&ctl->empty[stage], 0x3);
           if (++stage == PR_STAGES) stage = 0, phase ^= 1;
@@ -604,9 +701,13 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_pair_kernel(const __grid_cons
     const int r_local = quarter * 32 + lane;
     const uint32_t t_lane = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16);
     int local = 0;
-    for (int t = pair; t < tiles; t += num_pairs, ++local) {
+    PairIter it;
+    it.init(p, pair);
+    PairWork w;
+    const int split = static_cast<int>(p.sk_units);
+    for (; it.next(p, pair, num_pairs, w); ++local) {
       int mb, nb;
-      tile_coords(t, p.num_m, p.num_n, mb, nb);
+      tile_coords(w.tile, p.num_m, p.num_n, mb, nb);
       const int acc = local & 1;
       const uint32_t acc_phase = (local >> 1) & 1;
       if (!mbar_wait_bounded(&ctl->acc_full[acc], acc_phase, p.wait_limit, abort_flag)) {
@@ -615,25 +716,94 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_pair_kernel(const __grid_cons
       }
       __syncwarp();
       tc_fence_after();
+      const uint32_t acc_emp = mapa_shared(smem_u32(&ctl->acc_empty[acc]), 0);
+      if (w.piece > 0) {
+        // Contributor: raw partial sums of this CTA's 128 rows -> workspace slot, then its flag.
+        // Slot layout [column quad][row][4]: a warp's float4 stores are 512 contiguous bytes.
+        const int slot = (w.slot + w.piece - 1) * 2 + static_cast<int>(rank);
+        float4* dst = reinterpret_cast<float4*>(p.ws + static_cast<size_t>(slot) * SK_SLOT_FLOATS) + r_local;
+        for (int chunk = 0; chunk < BN / 32; ++chunk) {
+          uint32_t r[32];
+          tmem_ld_32x32b_x32(t_lane + acc * BN + chunk * 32, r);
+          tc_wait_ld();
+#pragma unroll
+          for (int j = 0; j < 32; j += 4)
+            __stcg(dst + static_cast<size_t>(chunk * 8 + j / 4) * PR_BM,
+                   make_float4(__uint_as_float(r[j]), __uint_as_float(r[j + 1]), __uint_as_float(r[j + 2]),
+                               __uint_as_float(r[j + 3])));
+        }
+        __threadfence();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) {
+          mbar_arrive_cluster(acc_emp);
+          mbar_arrive(&ctl->sk_stored);
+        }
+        if (warp == 2 && lane == 0) {
+          if (mbar_wait_bounded(&ctl->sk_stored, 0, p.wait_limit, abort_flag)) {
+            __threadfence();
+            atomicExch(p.flags + slot, 1u);
+          } else if (!*abort_flag) {
+            pair_abort(ctl, NTL_STATUS_ACC_FULL_WAIT);
+          }
+        }
+        continue;
+      }
+      const bool finalise = w.k1 < p.kb;  // piece 0 of a split tile
+      if (finalise) {
+        bool ready = true;
+        for (int pc = 1; pc < split && ready; ++pc) {
+          if (lane == 0) ready = wait_flag(p.flags + (w.slot + pc - 1) * 2 + rank, p.wait_limit, abort_flag);
+          ready = __shfl_sync(0xffffffffu, ready ? 1 : 0, 0) != 0;
+        }
+        if (!ready) {
+          if (!*abort_flag) pair_abort(ctl, NTL_STATUS_ACC_FULL_WAIT);
+          break;
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&ctl->sk_read);
+      }
       const int row = mb * PR_TILE_M + static_cast<int>(rank) * PR_BM + r_local;
       const bool row_ok = row < p.M;
       float* crow = p.c + static_cast<int64_t>(row) * p.N;
       const float row_bias = (p.bias_mode == NTL_BIAS_M && row_ok) ? __ldg(p.bias + row) : 0.0f;
+      float* bias_s = reinterpret_cast<float*>(smem + PR_STAGES * PR_STAGE_BYTES + 1024) + (warp - 2) * BN;
+      if (p.bias_mode == NTL_BIAS_N) stage_bias_n(p, nb * BN, bias_s, lane);
       for (int chunk = 0; chunk < BN / 32; ++chunk) {
         const int col0 = nb * BN + chunk * 32;
         if (col0 >= p.N) break;
         uint32_t r[32];
         tmem_ld_32x32b_x32(t_lane + acc * BN + chunk * 32, r);
         tc_wait_ld();
-        if (!row_ok) continue;
         float v[32];
 #pragma unroll
         for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
-        store_row_chunk(v, p, row, col0, crow, row_bias);
+        if (finalise) {
+          for (int pc = 1; pc < split; ++pc) {
+            const int slot = (w.slot + pc - 1) * 2 + static_cast<int>(rank);
+            const float4* part =
+                reinterpret_cast<const float4*>(p.ws + static_cast<size_t>(slot) * SK_SLOT_FLOATS) + r_local;
+#pragma unroll
+            for (int j = 0; j < 32; j += 4) {
+              const float4 q = __ldcg(part + static_cast<size_t>(chunk * 8 + j / 4) * PR_BM);
+              v[j] += q.x, v[j + 1] += q.y, v[j + 2] += q.z, v[j + 3] += q.w;
+            }
+          }
+        }
+        if (!row_ok) continue;
+        store_row_chunk(v, p, row, col0, crow, row_bias, bias_s + chunk * 32);
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_u32(&ctl->acc_empty[acc]), 0));
+      if (lane == 0) mbar_arrive_cluster(acc_emp);
+      if (finalise && warp == 2 && lane == 0) {
+        // Every epilogue warp has seen the flags: reset them for the next launch.
+        if (mbar_wait_bounded(&ctl->sk_read, 0, p.wait_limit, abort_flag)) {
+          for (int pc = 1; pc < split; ++pc) atomicExch(p.flags + (w.slot + pc - 1) * 2 + rank, 0u);
+        } else if (!*abort_flag) {
+          pair_abort(ctl, NTL_STATUS_ACC_FULL_WAIT);
+        }
+      }
     }
   }
 
@@ -798,16 +968,62 @@ int pair_clusters(int* clusters_out) {
   return NTL_OK;
 }
 
-int gemm_pair_launch(const uint16_t* a, const uint16_t* b, GemmParams p, cudaStream_t s) {
+// Work plan of the pair kernel.  With a workspace, the tiles of the last partial wave are
+// split along K over the otherwise idle pairs (2 to 4 pieces of at least 4 k-blocks each).
+struct PairPlan {
+  int num_m, num_n, tiles, kb, pairs, dp_tiles, split, split_pairs;
+  size_t ws_bytes;
+};
+
+constexpr int PR_MAX_SPLIT = 4, PR_MIN_PIECE_KB = 4;
+
+int make_pair_plan(int64_t M, int64_t N, int64_t K, bool split_tail, PairPlan* pl) {
   int clusters = 0;
   if (int rc = pair_clusters(&clusters)) return rc;
-  p.num_m = static_cast<int>((p.M + PR_TILE_M - 1) / PR_TILE_M);
-  p.num_n = static_cast<int>((p.N + BN - 1) / BN);
-  p.kb = static_cast<int>((p.K + BK - 1) / BK);
-  const int64_t tiles = static_cast<int64_t>(p.num_m) * p.num_n;
+  pl->num_m = static_cast<int>((M + PR_TILE_M - 1) / PR_TILE_M);
+  pl->num_n = static_cast<int>((N + BN - 1) / BN);
+  const int64_t tiles = static_cast<int64_t>(pl->num_m) * pl->num_n;
   NTL_REQUIRE(tiles < (int64_t(1) << 31), NTL_ERR_UNSUPPORTED, "gemm: too many tiles");
-  p.dp_tiles = static_cast<int>(tiles);
-  p.sk_ctas = 0, p.sk_units = 0, p.ws = nullptr, p.flags = nullptr;
+  pl->tiles = static_cast<int>(tiles);
+  pl->kb = static_cast<int>((K + BK - 1) / BK);
+  pl->pairs = static_cast<int>(tiles < clusters ? tiles : clusters);
+  pl->dp_tiles = pl->tiles;
+  pl->split = 1;
+  pl->split_pairs = 0;
+  pl->ws_bytes = 0;
+  const int left = pl->tiles % clusters;
+  if (split_tail && left > 0) {
+    int split = clusters / left;
+    if (split > PR_MAX_SPLIT) split = PR_MAX_SPLIT;
+    while (split >= 2 && pl->kb / split < PR_MIN_PIECE_KB) --split;
+    if (split >= 2 && static_cast<size_t>(left) * (split - 1) * 2 > kWsMaxSlots) split = 1;
+    if (split >= 2) {
+      pl->pairs = clusters;
+      pl->dp_tiles = pl->tiles - left;
+      pl->split = split;
+      pl->split_pairs = left * split;
+      const size_t slots = static_cast<size_t>(left) * (split - 1) * 2;  // one per CTA half
+      pl->ws_bytes = kWsFlagBytes + slots * SK_SLOT_FLOATS * sizeof(float);
+    }
+  }
+  return NTL_OK;
+}
+
+int gemm_pair_launch(const uint16_t* a, const uint16_t* b, GemmParams p, void* ws, size_t ws_bytes, bool split_tail,
+                     cudaStream_t s) {
+  PairPlan pl;
+  if (int rc = make_pair_plan(p.M, p.N, p.K, split_tail, &pl)) return rc;
+  if (pl.split > 1) {
+    NTL_REQUIRE(ws != nullptr && ws_bytes >= pl.ws_bytes, NTL_ERR_INVALID,
+                "gemm: workspace of %zu bytes needed, %zu given", pl.ws_bytes, ws_bytes);
+    NTL_REQUIRE(ntl_aligned(ws, 16), NTL_ERR_ALIGNMENT, "gemm: workspace must be 16-byte aligned");
+  }
+  p.num_m = pl.num_m, p.num_n = pl.num_n, p.kb = pl.kb;
+  p.dp_tiles = pl.dp_tiles;
+  p.sk_ctas = pl.split_pairs;
+  p.sk_units = pl.split;
+  p.ws = pl.split > 1 ? reinterpret_cast<float*>(static_cast<unsigned char*>(ws) + kWsFlagBytes) : nullptr;
+  p.flags = pl.split > 1 ? static_cast<uint32_t*>(ws) : nullptr;
   CUtensorMap ma, mb;
   if (int rc = make_map_f16(&ma, a, p.M, p.K, BK, PR_BM)) return rc;
   if (p.b_trans) {
@@ -815,9 +1031,8 @@ int gemm_pair_launch(const uint16_t* a, const uint16_t* b, GemmParams p, cudaStr
   } else {
     if (int rc = make_map_f16(&mb, b, p.K, p.N, 64, BK)) return rc;
   }
-  const int pairs = static_cast<int>(tiles < clusters ? tiles : clusters);
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(static_cast<unsigned>(2 * pairs), 1, 1);
+  cfg.gridDim = dim3(static_cast<unsigned>(2 * pl.pairs), 1, 1);
   cfg.blockDim = dim3(THREADS, 1, 1);
   cfg.dynamicSmemBytes = PR_SMEM_BYTES;
   cfg.stream = s;
@@ -856,13 +1071,13 @@ int make_plan(int64_t M, int64_t N, int64_t K, bool stream_k, Plan* pl) {
   if (stream_k && pl->tiles % sms != 0) {
     const int dp = (pl->tiles / sms) * sms;
     const int64_t units = static_cast<int64_t>(pl->tiles - dp) * pl->kb;
-    const int64_t ctas = std::min<int64_t>(sms, units / SK_MIN_UNITS);
+    const int64_t ctas = std::min<int64_t>(std::min<int64_t>(sms, units / SK_MIN_UNITS), kWsMaxSlots);
     if (ctas >= 2) {
       pl->grid = sms;
       pl->dp_tiles = dp;
       pl->sk_units = units;
       pl->sk_ctas = static_cast<int>(ctas);
-      pl->ws_bytes = static_cast<size_t>(ctas) * SK_SLOT_FLOATS * sizeof(float) + static_cast<size_t>(ctas) * 4;
+      pl->ws_bytes = kWsFlagBytes + static_cast<size_t>(ctas) * SK_SLOT_FLOATS * sizeof(float);
     }
   }
   return NTL_OK;
@@ -888,6 +1103,7 @@ int gemm_launch(const uint16_t* a, const uint16_t* b, float* c, const float* bia
   p.M = static_cast<int>(M), p.N = static_cast<int>(N), p.K = static_cast<int>(K);
   p.b_trans = b_trans ? 1 : 0;
   p.vec_store = (N % 4 == 0 && ntl_aligned(c, 16)) ? 1 : 0;
+  p.vec_bias = (bias != nullptr && N % 4 == 0 && ntl_aligned(bias, 16)) ? 1 : 0;
   p.wait_limit = ntl_wait_limit();
   const bool tma_ok = K > 0 && K % 8 == 0 && (b_trans || N % 8 == 0) && ntl_aligned(a, 16) && ntl_aligned(b, 16);
   if (!tma_ok) {
@@ -897,7 +1113,7 @@ int gemm_launch(const uint16_t* a, const uint16_t* b, float* c, const float* bia
     ntl_note_launch();
     return ntl_check_launch("gemm (CUDA-core path) launch");
   }
-  if (!stream_k && M > PR_BM) return gemm_pair_launch(a, b, p, s);
+  if (M > PR_BM) return gemm_pair_launch(a, b, p, ws, ws_bytes, stream_k, s);
   Plan pl;
   if (int rc = make_plan(M, N, K, stream_k, &pl)) return rc;
   if (pl.sk_ctas > 0) {
@@ -909,9 +1125,8 @@ int gemm_launch(const uint16_t* a, const uint16_t* b, float* c, const float* bia
   p.dp_tiles = pl.dp_tiles;
   p.sk_ctas = pl.sk_ctas;
   p.sk_units = pl.sk_units;
-  p.ws = static_cast<float*>(ws);
-  p.flags = pl.sk_ctas > 0 ? reinterpret_cast<uint32_t*>(static_cast<float*>(ws) + pl.sk_ctas * SK_SLOT_FLOATS)
-                           : nullptr;
+  p.ws = pl.sk_ctas > 0 ? reinterpret_cast<float*>(static_cast<unsigned char*>(ws) + kWsFlagBytes) : nullptr;
+  p.flags = pl.sk_ctas > 0 ? static_cast<uint32_t*>(ws) : nullptr;
   CUtensorMap ma, mb;
   if (int rc = make_map_f16(&ma, a, M, K, BK, BM)) return rc;
   if (b_trans) {
@@ -949,6 +1164,12 @@ extern "C" int ntl_gemm_workspace_size(int64_t M, int64_t N, int64_t K, int b_tr
   NTL_REQUIRE(M >= 0 && N >= 0 && K >= 0, NTL_ERR_INVALID, "gemm_workspace_size: negative size");
   *bytes_out = 0;
   if (M == 0 || N == 0 || K == 0 || K % 8 != 0 || (!b_trans && N % 8 != 0)) return NTL_OK;
+  if (M > PR_BM) {
+    PairPlan pp;
+    if (int rc = make_pair_plan(M, N, K, true, &pp)) return rc;
+    *bytes_out = pp.ws_bytes;
+    return NTL_OK;
+  }
   Plan pl;
   if (int rc = make_plan(M, N, K, true, &pl)) return rc;
   *bytes_out = pl.ws_bytes;
@@ -967,12 +1188,13 @@ extern "C" int ntl_gemm_f16_f32_ws(const uint16_t* a, const uint16_t* b, float* 
 // Some callers cannot allocate device memory for a workspace: a plugin host that hands a
 // kernel only its tensors and a stream (the reference's TVM-FFI launch path, for one, has no
 // workspace argument), or a runtime that runs with the device allocator switched off after
-// start-up.  ntl_gemm_f16_f32_noalloc gives them the stream-K GEMM with its scratch in a
+// start-up.  ntl_gemm_f16_f32_noalloc gives them the split-K GEMM with its scratch in a
 // file-scope device array instead of a caller buffer.
 //
 // The array is a fixed 16 MiB that every GPU loading this library holds until the process
-// exits.  Shapes whose stream-K plan needs more (4096^3 on a 148-SM B200 needs ~19 MB) are
-// rejected with NTL_ERR_UNSUPPORTED.  All calls share the array: the flag words are cleared
+// exits.  Shapes whose plan needs more are rejected with NTL_ERR_UNSUPPORTED: split tails of
+// the CTA-pair kernel (M > 128) need at most ~15 MB, but a one-SM stream-K plan for M <= 128
+// can need up to 148 slots of 128 KB (128 x 25600 x 4096 needs ~19 MB).  All calls share the array: the flag words are cleared
 // (cudaMemsetAsync on the caller's stream) before every launch, and calls that overlap on
 // the GPU race on it.  Host code cannot pass the array's name to a kernel (on the host it
 // is a stand-in, not a device address), so the first call on each device looks up its
@@ -1015,12 +1237,8 @@ extern "C" int ntl_gemm_f16_f32_noalloc(const uint16_t* a, const uint16_t* b, fl
   if (int rc = noalloc_scratch(&scratch)) return rc;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (need > 0) {
-    // The plan's flag words follow its partial-sum slots; they must start at zero.
-    Plan pl;
-    if (int rc = make_plan(M, N, K, true, &pl)) return rc;
-    const size_t flags_off = static_cast<size_t>(pl.sk_ctas) * SK_SLOT_FLOATS * sizeof(float);
-    cudaError_t e = cudaMemsetAsync(static_cast<unsigned char*>(scratch) + flags_off, 0,
-                                    static_cast<size_t>(pl.sk_ctas) * 4, s);
+    // The flag block at the front of the workspace must start at zero.
+    cudaError_t e = cudaMemsetAsync(scratch, 0, kWsFlagBytes, s);
     if (e != cudaSuccess) return ntl_fail(NTL_ERR_CUDA, "gemm_noalloc: clearing flags: %s", cudaGetErrorString(e));
   }
   return gemm_launch(a, b, c, bias, bias_mode, alpha, relu, M, N, K, b_trans, need > 0 ? scratch : nullptr,

@@ -25,8 +25,9 @@ _workspaces: dict = {}
 def gemm_workspace(device, nbytes: int):
     """A zero-initialised workspace of at least ``nbytes`` on ``device``, cached per device.
 
-    The stream-K GEMM leaves its flag words zero after every successful call, so the buffer
-    is reused as is.  Calls that share it run in stream order on the caller's stream.
+    The split-K GEMM keeps its flag words in the first 4 KB of every workspace and leaves
+    them zero after every successful call, so the buffer is reused as is for any shape that
+    fits.  Calls that share it run in stream order on the caller's stream.
     """
     import torch
 

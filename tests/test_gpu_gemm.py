@@ -171,6 +171,29 @@ def test_gemm_stream_k_repeated_calls(torch_cuda, m, n, k):
         check(torch, c, ref)
 
 
+@pytest.mark.parametrize("m,n,k", [(4096, 4096, 4096), (520, 2048, 1024), (96, 4096, 2048)])
+def test_gemm_split_tail_transpose_b_row_bias(torch_cuda, m, n, k):
+    """The split tail with B given as [N, K], a per-row bias and alpha = 0.5 (CTA-pair kernel for
+    M > 128, one-SM stream-K for M <= 128)."""
+    torch = torch_cuda
+    from ntilang_b200 import _lib
+
+    from ntilang_b200.launch import gemm_workspace
+
+    need = _lib.gemm_workspace_size(m, n, k, 1)
+    ws = gemm_workspace(torch.device("cuda"), need)
+    gen = torch.Generator(device="cuda").manual_seed(m)
+    a = (torch.randn(m, k, device="cuda", generator=gen) / k**0.5).half()
+    b = torch.randn(n, k, device="cuda", generator=gen).half()
+    bias = torch.randn(m, device="cuda", generator=gen)
+    ref = torch.relu(ref_gemm(torch, a, b, trans_b=True) * 0.5 + bias[:, None])
+    for _ in range(2):
+        c = torch.full((m, n), float("nan"), device="cuda")
+        _lib.call("ntl_gemm_f16_f32_ws", a.data_ptr(), b.data_ptr(), c.data_ptr(), bias.data_ptr(), 3, 0.5, 1, m, n,
+                  k, 1, ws.data_ptr(), ws.numel(), torch.cuda.current_stream().cuda_stream)
+        check(torch, c, ref)
+
+
 def test_gemm_stream_k_matches_data_parallel_entry(torch_cuda):
     torch = torch_cuda
     from ntilang_b200 import _lib

@@ -3,7 +3,7 @@
 It exists for callers that cannot allocate device memory for a workspace: a plugin host
 that hands a kernel only tensors and a stream (the reference's TVM-FFI launch path has no
 workspace argument), or a runtime that runs with the device allocator switched off.  It
-runs the same stream-K GEMM as ntl_gemm_f16_f32_ws, with the scratch in a fixed 16 MiB
+runs the same split-K GEMM as ntl_gemm_f16_f32_ws, with the scratch in a fixed 16 MiB
 device array inside the library instead of a caller buffer.
 
 The test calls it through the C ABI twice in a row (the array keeps the previous call's
@@ -31,7 +31,7 @@ def test_noalloc_gemm_matches_workspace_entry_point(torch_cuda):
     torch = torch_cuda
     from ntilang_b200 import _lib
 
-    m, n, k = 1536, 4096, 1024  # a data-parallel wave plus a stream-K tail of 44 tiles
+    m, n, k = 1536, 4096, 1024  # one wave of 74 pair tiles, then 22 tail tiles split in 3 along K
     need = _lib.gemm_workspace_size(m, n, k, 0)
     assert 0 < need <= 16 << 20
     stream = torch.cuda.current_stream().cuda_stream
@@ -58,9 +58,9 @@ def test_noalloc_gemm_refuses_plans_larger_than_its_scratch(torch_cuda):
     torch = torch_cuda
     from ntilang_b200 import _lib
 
-    m = n = k = 4096
+    m, n, k = 128, 25600, 4096  # one-SM stream-K plan over every SM: 148 slots of 128 KB
     if _lib.gemm_workspace_size(m, n, k, 0) <= 16 << 20:
-        pytest.skip("this device's stream-K plan for 4096^3 fits the static scratch")
+        pytest.skip("this device's plan for 128x25600x4096 fits the static scratch")
     a = torch.zeros(m, k, device="cuda").half()
     b = torch.zeros(k, n, device="cuda").half()
     c = torch.empty(m, n, device="cuda")
