@@ -21,7 +21,10 @@
 namespace {
 
 constexpr unsigned kFull = 0xffffffffu;
-constexpr int kWarpsPerBlock = 8;
+// Rows (warps) per block of the warp-per-row kernels, measured per op on B200 at the BASELINE
+// shapes: softmax 16384x512 is fastest with 8, RMSNorm 4096x1024 with 16 (6.4 vs 6.8 us).
+constexpr int kSoftmaxWarpsPerBlock = 8;
+constexpr int kRmsnormWarpsPerBlock = 16;
 
 template <bool VEC>
 __device__ __forceinline__ void load4(const float* __restrict__ row, int64_t col, int64_t cols, float pad,
@@ -88,11 +91,11 @@ __device__ __forceinline__ float chunk_tree(float (&s)[N]) {
 // ------------------------------------------------------------------------- softmax
 
 template <int NCH, bool VEC>
-__global__ void __launch_bounds__(kWarpsPerBlock * 32) softmax_rows_warp(const float* __restrict__ x,
+__global__ void __launch_bounds__(kSoftmaxWarpsPerBlock * 32) softmax_rows_warp(const float* __restrict__ x,
                                                                          float* __restrict__ y, int64_t rows,
                                                                          int64_t cols) {
   const int lane = threadIdx.x & 31;
-  const int64_t row = static_cast<int64_t>(blockIdx.x) * kWarpsPerBlock + (threadIdx.x >> 5);
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * kSoftmaxWarpsPerBlock + (threadIdx.x >> 5);
   if (lane == 0 && row < rows) prefetch_l2(x + row * cols, cols * 4);
   pdl_wait();
   pdl_trigger();
@@ -180,12 +183,12 @@ __global__ void __launch_bounds__(256) softmax_rows_cta(const float* __restrict_
 // ------------------------------------------------------------------------- RMSNorm
 
 template <int NCH, bool VEC>
-__global__ void __launch_bounds__(kWarpsPerBlock * 32) rmsnorm_rows_warp(const float* __restrict__ x,
+__global__ void __launch_bounds__(kRmsnormWarpsPerBlock * 32) rmsnorm_rows_warp(const float* __restrict__ x,
                                                                          const float* __restrict__ w,
                                                                          float* __restrict__ y, int64_t rows,
                                                                          int64_t cols, float eps, float inv_n) {
   const int lane = threadIdx.x & 31;
-  const int64_t row = static_cast<int64_t>(blockIdx.x) * kWarpsPerBlock + (threadIdx.x >> 5);
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * kRmsnormWarpsPerBlock + (threadIdx.x >> 5);
   if (lane == 0 && row < rows) prefetch_l2(x + row * cols, cols * 4);
   if (threadIdx.x == 32) prefetch_l2(w, cols * 4);
   pdl_wait();
@@ -271,13 +274,13 @@ constexpr int64_t kMaxCtaCols = 16384;   // 16 chunks of 1024 per CTA
 template <class WarpK, class CtaK>
 struct Dispatch;
 
-#define NTL_ROW_DISPATCH(KW, KC, VEC, ...)                                                              \
+#define NTL_ROW_DISPATCH(KW, KC, VEC, WPB, ...)                                                         \
   do {                                                                                                  \
     const int64_t nch = (cols + 127) / 128;                                                             \
     if (cols <= kMaxWarpCols) {                                                                         \
-      const int64_t blocks = (rows + kWarpsPerBlock - 1) / kWarpsPerBlock;                              \
+      const int64_t blocks = (rows + (WPB)-1) / (WPB);                                                  \
       NTL_REQUIRE(blocks <= 0x7fffffff, NTL_ERR_UNSUPPORTED, "too many rows");                         \
-      dim3 g(static_cast<unsigned>(blocks)), b(kWarpsPerBlock * 32);                                    \
+      dim3 g(static_cast<unsigned>(blocks)), b((WPB)*32);                                               \
       if (nch <= 1) ntl_launch_pdl(KW<1, VEC>, g, b, 0, s, __VA_ARGS__);                                \
       else if (nch <= 2) ntl_launch_pdl(KW<2, VEC>, g, b, 0, s, __VA_ARGS__);                           \
       else if (nch <= 4) ntl_launch_pdl(KW<4, VEC>, g, b, 0, s, __VA_ARGS__);                           \
@@ -305,9 +308,9 @@ extern "C" int ntl_softmax_f32(const float* x, float* y, int64_t rows, int64_t c
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const bool vec = (cols % 4 == 0) && ntl_aligned(x, 16) && ntl_aligned(y, 16);
   if (vec)
-    NTL_ROW_DISPATCH(softmax_rows_warp, softmax_rows_cta, true, x, y, rows, cols);
+    NTL_ROW_DISPATCH(softmax_rows_warp, softmax_rows_cta, true, kSoftmaxWarpsPerBlock, x, y, rows, cols);
   else
-    NTL_ROW_DISPATCH(softmax_rows_warp, softmax_rows_cta, false, x, y, rows, cols);
+    NTL_ROW_DISPATCH(softmax_rows_warp, softmax_rows_cta, false, kSoftmaxWarpsPerBlock, x, y, rows, cols);
   ntl_note_launch();
   return ntl_check_launch("softmax launch");
 }
@@ -322,9 +325,9 @@ extern "C" int ntl_rmsnorm_f32(const float* x, const float* w, float* y, int64_t
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const bool vec = (cols % 4 == 0) && ntl_aligned(x, 16) && ntl_aligned(y, 16) && ntl_aligned(w, 16);
   if (vec)
-    NTL_ROW_DISPATCH(rmsnorm_rows_warp, rmsnorm_rows_cta, true, x, w, y, rows, cols, eps, inv_n);
+    NTL_ROW_DISPATCH(rmsnorm_rows_warp, rmsnorm_rows_cta, true, kRmsnormWarpsPerBlock, x, w, y, rows, cols, eps, inv_n);
   else
-    NTL_ROW_DISPATCH(rmsnorm_rows_warp, rmsnorm_rows_cta, false, x, w, y, rows, cols, eps, inv_n);
+    NTL_ROW_DISPATCH(rmsnorm_rows_warp, rmsnorm_rows_cta, false, kRmsnormWarpsPerBlock, x, w, y, rows, cols, eps, inv_n);
   ntl_note_launch();
   return ntl_check_launch("rmsnorm launch");
 }
