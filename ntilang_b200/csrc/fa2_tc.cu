@@ -7,15 +7,18 @@
 // statistics (codegen.py:972-984, :1062-1073).
 //
 // Design: one CTA = one (batch, head, 256-query block) = two 128-row query tiles that
-// share every K/V tile (576 threads, 18 warps):
-//   warps 0-7   softmax, O rescale and the O / l -> fp16 epilogue of query tile 0: each warp
-//               owns 16 TMEM lanes (rows) x all 128 keys of S; through 16x256b accesses the
-//               four threads of a row sit in one warp (row max / sum by two shuffles)
-//   warps 8-15  the same for query tile 1
-//   warp 16     TMEM owner (512 columns: S0, S1, O0, O1) and MMA issuer
-//   warp 17     TMA: Q0, Q1 once, then K_j and V_j (2-stage rings each) with K running one
+// share every K/V tile (384 threads, 12 warps = 3 warpgroups):
+//   warps 0-3   softmax, O rescale and the O / l -> fp16 epilogue of query tile 0: one thread
+//               per query row (its TMEM lane), the row's 128 scores in registers
+//   warps 4-7   the same for query tile 1
+//   warp 8      TMEM owner (512 columns: S0, S1, O0, O1) and MMA issuer
+//   warp 9      TMA: Q0, Q1 once, then K_j and V_j (2-stage rings each) with K running one
 //               tile ahead; 3-D tensor maps [B*H, S, D] zero-fill rows past S and never
-//               cross heads.
+//               cross heads
+//   warps 10-11 idle (they complete warpgroup 2 for the register split)
+// Registers: launched at 168 per thread; warpgroup 2 gives up registers down to 72 and the
+// two softmax warpgroups take them, up to 216 (setmaxnreg), so a softmax thread holds its
+// row's scores, exponentials and packed P without spilling.
 // Per KV tile j the MMA warp issues, per query tile i: O_i += P_i V_j (A = P_i from TMEM,
 // fp16 pairs packed over the first 64 S_i columns; B = V_j N-major in smem) and then
 // S_i = Q_i K_{j+1}^T (both operands K-major in smem), so the tensor core works on one tile
@@ -43,9 +46,12 @@ constexpr int QTILES = 2;      // query tiles per CTA
 constexpr int BQ = BM * QTILES;
 constexpr int BN = 128;        // keys per KV tile
 constexpr int KSTAGES = 2, VSTAGES = 2;
-constexpr int THREADS = 576;
-constexpr int MMA_WARP = 16, TMA_WARP = 17;
-constexpr int SM_WARPS_PER_TILE = 8;  // two threads per query row (64 keys each)
+constexpr int THREADS = 384;  // 3 warpgroups: softmax tile 0, softmax tile 1, MMA + TMA (+2 idle)
+constexpr int REGS_LAUNCH = 168, REGS_SOFTMAX = 216, REGS_OTHER = 72;
+static_assert(8 * REGS_SOFTMAX + 4 * REGS_OTHER == 12 * REGS_LAUNCH, "register split must match the launch");
+static_assert(2 * REGS_SOFTMAX + REGS_OTHER <= 512, "per-SMSP register file");
+constexpr int MMA_WARP = 8, TMA_WARP = 9;
+constexpr int SM_WARPS_PER_TILE = 4;  // one thread per query row
 constexpr uint32_t TMEM_COLS = 512;
 constexpr float kRescaleLog2 = 8.0f;  // lazy-rescale threshold (log2 units)
 
@@ -64,11 +70,9 @@ struct __align__(16) Fa2Ctl {
   uint64_t sm_done[QTILES];
   uint64_t p_lo[QTILES];     // the low-key half of P_i is in TMEM (8 warps)
   uint64_t o_final[QTILES];
-  uint64_t l_ready[QTILES];  // the 8 softmax warps of a tile published their row sums
   uint64_t drain;
   uint32_t tmem_base;
   int abort;
-  float lsum[QTILES][BM];    // row sums l, written once per tile at the end
 };
 
 template <int D>
@@ -122,51 +126,6 @@ __device__ __forceinline__ void exp2_fma2(uint64_t x2, float& p0, float& p1) {
   p1 = __uint_as_float(__float_as_uint(q1) + (__float_as_uint(t1) << 23));
 }
 
-// Scores of keys >= lim (per row) become -inf.  v is one 16x256b.x8 load: v[4g + e] holds key
-// key0 + 8g + (e&1) of row A (e < 2, limit limA) or row B (limit limB).
-__device__ __forceinline__ void mask_keys(uint32_t (&v)[32], int key0, int limA, int limB) {
-#pragma unroll
-  for (int g = 0; g < 8; ++g) {
-    const int key = key0 + 8 * g;
-    if (key >= limA) v[4 * g] = __float_as_uint(-INFINITY);
-    if (key + 1 >= limA) v[4 * g + 1] = __float_as_uint(-INFINITY);
-    if (key >= limB) v[4 * g + 2] = __float_as_uint(-INFINITY);
-    if (key + 1 >= limB) v[4 * g + 3] = __float_as_uint(-INFINITY);
-  }
-}
-
-// p = exp2(s*c - m*c) for one 16x256b.x8 block of scores (64 keys of rows A and B), row
-// sums into sA2 / sB2 (f32x2 partials), fp16 pairs of consecutive keys stored with a
-// 16x128b.x8 access at `p_addr` (32 packed columns).
-__device__ __forceinline__ void exp_pack_store(const uint32_t (&v)[32], uint64_t c2, uint64_t nA2, uint64_t nB2,
-                                               uint64_t (&sA2)[2], uint64_t (&sB2)[2], uint32_t p_addr) {
-  uint32_t pk[16];
-#pragma unroll
-  for (int g = 0; g < 8; ++g) {
-    const uint64_t xA = f2_fma(f2_make(__uint_as_float(v[4 * g]), __uint_as_float(v[4 * g + 1])), c2, nA2);
-    const uint64_t xB = f2_fma(f2_make(__uint_as_float(v[4 * g + 2]), __uint_as_float(v[4 * g + 3])), c2, nB2);
-    float a0, a1, b0, b1;
-    if ((g & 3) == 3) {  // a fixed quarter of the exponentials on the FMA pipe
-      exp2_fma2(xA, a0, a1);
-      exp2_fma2(xB, b0, b1);
-    } else {
-      float x0, x1;
-      f2_split(xA, x0, x1);
-      a0 = ex2_approx(x0);
-      a1 = ex2_approx(x1);
-      f2_split(xB, x0, x1);
-      b0 = ex2_approx(x0);
-      b1 = ex2_approx(x1);
-    }
-    sA2[g & 1] = f2_add(sA2[g & 1], f2_make(a0, a1));
-    sB2[g & 1] = f2_add(sB2[g & 1], f2_make(b0, b1));
-    pk[2 * g] = pack_half2(a0, a1);
-    pk[2 * g + 1] = pack_half2(b0, b1);
-  }
-  tmem_st_16x128b_x8(p_addr, pk);
-}
-
-
 // Number of KV tiles query tile i of block qb needs (0 when the tile is past S).
 __device__ __forceinline__ int kv_tiles(const Fa2Params& p, int q0_tile) {
   if (q0_tile >= p.S) return 0;
@@ -210,7 +169,6 @@ __global__ void __launch_bounds__(THREADS, 1) fa2_fwd_kernel(const __grid_consta
       mbar_init(&ctl->sm_done[i], SM_WARPS_PER_TILE);
       mbar_init(&ctl->p_lo[i], SM_WARPS_PER_TILE);
       mbar_init(&ctl->o_final[i], 1);
-      mbar_init(&ctl->l_ready[i], SM_WARPS_PER_TILE);
     }
     mbar_init(&ctl->drain, 1);
     ctl->abort = 0;
@@ -228,6 +186,8 @@ __global__ void __launch_bounds__(THREADS, 1) fa2_fwd_kernel(const __grid_consta
   tc_fence_after();
   const uint32_t tmem = ctl->tmem_base;
 
+  if (warp >= 8) {
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;\n" ::"n"(REGS_OTHER) : "memory");
   if (warp == TMA_WARP) {
     // ------------------------------------------------------------------ TMA producer
     if (elect_one_lane()) {
@@ -361,32 +321,26 @@ __global__ void __launch_bounds__(THREADS, 1) fa2_fwd_kernel(const __grid_consta
           atomicCAS(&g_fa2_status, 0u, NTL_STATUS_DRAIN_WAIT);
       }
     }
-  } else if (warp < 2 * SM_WARPS_PER_TILE) {
+  }
+  } else {
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;\n" ::"n"(REGS_SOFTMAX) : "memory");
     // ------------------------------------------------------------------ softmax warps
-    // Warp w: query tile i = w/8, lane quarter q = w%4 (the TMEM lanes a warp may access) and
-    // sub-block sb = (w/4)%2: TMEM lanes 32q + 16sb .. +15, all BN keys.  Through 16x256b
-    // accesses thread t holds two rows (lanes +t/4 and +t/4+8) and, in each 8-key group, keys
-    // 2(t%4) and 2(t%4)+1; the four threads of a row are lanes t^1, t^2, t^3 of this warp, so
-    // row maxima and sums combine with two shuffles.  S stays in registers between the max
-    // and the exponentials; P (fp16 pairs of consecutive keys) is written back over the S
-    // columns this warp has already read.
-    const int i = warp >> 3;
+    // Warp w: query tile i = w/4; thread = row r = 32*(w%4) + lane = its TMEM lane (the lanes a
+    // warp may access), all BN keys of the row in registers: row max and sum need no exchange.
+    const int i = warp >> 2;
     const int quarter = warp & 3;
-    const int sb = (warp >> 2) & 1;
-    const int lane_base = 32 * quarter + 16 * sb;
-    const int rA = lane_base + (lane >> 2), rB = rA + 8;  // this thread's rows of the tile
-    const int cq = 2 * (lane & 3);
+    const int r = quarter * 32 + lane;
     const int tile_q0 = q0 + i * BM;
-    const uint32_t lane_off = static_cast<uint32_t>(lane_base) << 16;
+    const int qrow = tile_q0 + r;
+    const int n_mine = kv_tiles(p, tile_q0);
+    const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
     const uint32_t s_addr = tmem + lane_off + L::S_COL(i);
     const uint32_t o_addr = tmem + lane_off + L::O_COL(i);
     const float c = p.c;
-    const int limA = p.causal ? min(p.S, tile_q0 + rA + 1) : p.S;  // keys < lim are kept
-    const int limB = p.causal ? min(p.S, tile_q0 + rB + 1) : p.S;
-    float mA = -INFINITY, mB = -INFINITY;  // lazily updated row maxima
-    float lA = 0.0f, lB = 0.0f;            // this thread's share of the row sums
+    const int key_lim = p.causal ? min(p.S, qrow + 1) : p.S;  // keys < key_lim are kept
+    float m_use = -INFINITY, l = 0.0f;
     bool ok = true;
-    for (int j = 0; j < n_t[i]; ++j) {
+    for (int j = 0; j < n_mine; ++j) {
       if (!mbar_wait_bounded(&ctl->s_full[i], j & 1, p.wait_limit, abort_flag)) {
         if (!*abort_flag) fa2_abort(ctl, NTL_STATUS_SOFTMAX_WAIT);
         ok = false;
@@ -394,139 +348,117 @@ __global__ void __launch_bounds__(THREADS, 1) fa2_fwd_kernel(const __grid_consta
       }
       __syncwarp();
       tc_fence_after();
-      // Low keys [0, 64) stay in registers from the max pass to the exponentials; the high
-      // keys are loaded again afterwards (their S columns are untouched until their own P
-      // store, which goes to packed columns [32, 64), i.e. low-key S columns already read).
-      uint32_t lo[32];  // lo[4g + e]: key 8g + cq + (e&1) of row A (e < 2) or row B
-      float mxA, mxB;
-      const bool masked_tile = (j * BN + BN > p.S) || (p.causal && j * BN + BN - 1 > tile_q0);
-      {
-        uint32_t hi[32];
-        tmem_ld_16x256b_x8(s_addr, lo);
-        tmem_ld_16x256b_x8(s_addr + 64, hi);
-        tc_wait_ld();
-        if (masked_tile) {
-          mask_keys(lo, j * BN + cq, limA, limB);
-          mask_keys(hi, j * BN + 64 + cq, limA, limB);
-        }
-        float xa0 = -INFINITY, xa1 = -INFINITY, xb0 = -INFINITY, xb1 = -INFINITY;
+      uint32_t sv[BN];  // S[r, j*BN + k]
 #pragma unroll
-        for (int g = 0; g < 8; ++g) {
-          xa0 = fmax3(xa0, __uint_as_float(lo[4 * g]), __uint_as_float(lo[4 * g + 1]));
-          xb0 = fmax3(xb0, __uint_as_float(lo[4 * g + 2]), __uint_as_float(lo[4 * g + 3]));
-          xa1 = fmax3(xa1, __uint_as_float(hi[4 * g]), __uint_as_float(hi[4 * g + 1]));
-          xb1 = fmax3(xb1, __uint_as_float(hi[4 * g + 2]), __uint_as_float(hi[4 * g + 3]));
-        }
-        mxA = fmaxf(xa0, xa1);
-        mxB = fmaxf(xb0, xb1);
+      for (int ch = 0; ch < BN / 32; ++ch)
+        tmem_ld_32x32b_x32(s_addr + ch * 32, *reinterpret_cast<uint32_t(*)[32]>(sv + ch * 32));
+      tc_wait_ld();
+      if ((j * BN + BN > p.S) || (p.causal && j * BN + BN - 1 > tile_q0)) {
+#pragma unroll
+        for (int k = 0; k < BN; ++k)
+          if (j * BN + k >= key_lim) sv[k] = __float_as_uint(-INFINITY);
       }
-      mxA = fmaxf(mxA, __shfl_xor_sync(0xffffffffu, mxA, 1));
-      mxB = fmaxf(mxB, __shfl_xor_sync(0xffffffffu, mxB, 1));
-      mxA = fmaxf(mxA, __shfl_xor_sync(0xffffffffu, mxA, 2));
-      mxB = fmaxf(mxB, __shfl_xor_sync(0xffffffffu, mxB, 2));
-      // lazy max: the four threads of a row take the same decision from the same values
-      float rsA = 1.0f, rsB = 1.0f;
+      float mx;
+      {
+        float x[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+        for (int k = 0; k < BN; k += 8) {
+          x[0] = fmax3(x[0], __uint_as_float(sv[k]), __uint_as_float(sv[k + 1]));
+          x[1] = fmax3(x[1], __uint_as_float(sv[k + 2]), __uint_as_float(sv[k + 3]));
+          x[2] = fmax3(x[2], __uint_as_float(sv[k + 4]), __uint_as_float(sv[k + 5]));
+          x[3] = fmax3(x[3], __uint_as_float(sv[k + 6]), __uint_as_float(sv[k + 7]));
+        }
+        mx = fmax3(fmaxf(x[0], x[1]), x[2], x[3]);
+      }
+      // lazy max
+      float rs = 1.0f;
       bool moved = false;
       if (j == 0) {
-        mA = mxA;
-        mB = mxB;
-      } else {
-        if ((mxA - mA) * c > kRescaleLog2) {
-          rsA = ex2_approx((mA - mxA) * c);
-          mA = mxA;
-          moved = true;
-        }
-        if ((mxB - mB) * c > kRescaleLog2) {
-          rsB = ex2_approx((mB - mxB) * c);
-          mB = mxB;
-          moved = true;
-        }
+        m_use = mx;
+      } else if ((mx - m_use) * c > kRescaleLog2) {
+        rs = ex2_approx((m_use - mx) * c);
+        m_use = mx;
+        moved = true;
       }
       if (__any_sync(0xffffffffu, moved)) {
         // O_i = P_{<j} V is complete: S_i of this tile was issued after the last P_i V.
 #pragma unroll 1
-        for (int ch = 0; ch < D / 64; ++ch) {
+        for (int ch = 0; ch < D / 32; ++ch) {
           uint32_t o[32];
-          tmem_ld_16x256b_x8(o_addr + ch * 64, o);
+          tmem_ld_32x32b_x32(o_addr + ch * 32, o);
           tc_wait_ld();
 #pragma unroll
-          for (int g = 0; g < 8; ++g) {
-            o[4 * g] = __float_as_uint(__uint_as_float(o[4 * g]) * rsA);
-            o[4 * g + 1] = __float_as_uint(__uint_as_float(o[4 * g + 1]) * rsA);
-            o[4 * g + 2] = __float_as_uint(__uint_as_float(o[4 * g + 2]) * rsB);
-            o[4 * g + 3] = __float_as_uint(__uint_as_float(o[4 * g + 3]) * rsB);
-          }
-          tmem_st_16x256b_x8(o_addr + ch * 64, o);
+          for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * rs);
+          tmem_st_32x32b_x32(o_addr + ch * 32, o);
         }
       }
-      // p = exp2(s*c - m*c) -> fp16 pairs; keys [64hf, 64hf + 64) -> packed columns [32hf, 32hf + 32)
+      // p = exp2(s*c - m*c) -> fp16 pairs: keys 2u, 2u+1 in S column u (columns already read)
       const uint64_t c2 = f2_make(c, c);
-      const uint64_t nA2 = f2_make(-mA * c, -mA * c), nB2 = f2_make(-mB * c, -mB * c);
-      uint64_t sA2[2] = {0ull, 0ull}, sB2[2] = {0ull, 0ull};
-      {
-        uint32_t hi[32];
-        tmem_ld_16x256b_x8(s_addr + 64, hi);
-        exp_pack_store(lo, c2, nA2, nB2, sA2, sB2, s_addr);
-        tc_wait_st();
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&ctl->p_lo[i]);
-        tc_wait_ld();
-        if (masked_tile) mask_keys(hi, j * BN + 64 + cq, limA, limB);
-        exp_pack_store(hi, c2, nA2, nB2, sA2, sB2, s_addr + 32);
+      const uint64_t nm2 = f2_make(-m_use * c, -m_use * c);
+      uint64_t acc2[2] = {0ull, 0ull};
+#pragma unroll
+      for (int ch = 0; ch < BN / 32; ++ch) {
+        uint32_t pk[16];
+#pragma unroll
+        for (int e = 0; e < 16; ++e) {
+          const int k = ch * 32 + 2 * e;
+          const uint64_t x2 = f2_fma(f2_make(__uint_as_float(sv[k]), __uint_as_float(sv[k + 1])), c2, nm2);
+          float p0, p1;
+          if ((e & 3) == 3) {  // one pair in four on the FMA pipe
+            exp2_fma2(x2, p0, p1);
+          } else {
+            float x0, x1;
+            f2_split(x2, x0, x1);
+            p0 = ex2_approx(x0);
+            p1 = ex2_approx(x1);
+          }
+          acc2[e & 1] = f2_add(acc2[e & 1], f2_make(p0, p1));
+          pk[e] = pack_half2(p0, p1);
+        }
+        tmem_st_32x32b_x16(s_addr + ch * 16, pk);
+        if (ch == BN / 64 - 1) {
+          // keys [0, BN/2) of P are in TMEM: the MMA warp may start on them
+          tc_wait_st();
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&ctl->p_lo[i]);
+        }
       }
-      float sumA, sumB;
+      float sum;
       {
         float u0, u1;
-        f2_split(f2_add(sA2[0], sA2[1]), u0, u1);
-        sumA = u0 + u1;
-        f2_split(f2_add(sB2[0], sB2[1]), u0, u1);
-        sumB = u0 + u1;
+        f2_split(f2_add(acc2[0], acc2[1]), u0, u1);
+        sum = u0 + u1;
       }
-      lA = (j == 0) ? sumA : __fmaf_rn(lA, rsA, sumA);
-      lB = (j == 0) ? sumB : __fmaf_rn(lB, rsB, sumB);
+      l = (j == 0) ? sum : __fmaf_rn(l, rs, sum);
       tc_wait_st();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&ctl->sm_done[i]);
     }
-    // epilogue: row sums to shared memory, then O / l -> fp16 with 32x32b accesses (thread =
-    // row 32q + lane, columns [sb*D/2, sb*D/2 + D/2)).
-    if (ok && n_t[i] > 0) {
-      lA += __shfl_xor_sync(0xffffffffu, lA, 1);
-      lB += __shfl_xor_sync(0xffffffffu, lB, 1);
-      lA += __shfl_xor_sync(0xffffffffu, lA, 2);
-      lB += __shfl_xor_sync(0xffffffffu, lB, 2);
-      if ((lane & 3) == 0) {
-        ctl->lsum[i][rA] = lA;
-        ctl->lsum[i][rB] = lB;
-      }
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&ctl->l_ready[i]);
-      const int r = quarter * 32 + lane;
-      const int qrow = tile_q0 + r;
-      const uint32_t o_row = tmem + (static_cast<uint32_t>(quarter * 32) << 16) + L::O_COL(i) + sb * (D / 2);
-      if (!mbar_wait_bounded(&ctl->l_ready[i], 0, p.wait_limit, abort_flag) ||
-          !mbar_wait_bounded(&ctl->o_final[i], 0, p.wait_limit, abort_flag)) {
+    // epilogue: O / l -> fp16, the thread's row
+    if (ok && n_mine > 0) {
+      if (!mbar_wait_bounded(&ctl->o_final[i], 0, p.wait_limit, abort_flag)) {
         if (!*abort_flag) fa2_abort(ctl, NTL_STATUS_SOFTMAX_WAIT);
       } else {
         __syncwarp();
         tc_fence_after();
-        const float inv_l = 1.0f / ctl->lsum[i][r];
-        __half* orow = p.o + (static_cast<int64_t>(bh) * p.S + qrow) * D + sb * (D / 2);
+        const float inv_l = 1.0f / l;
+        __half* orow = p.o + (static_cast<int64_t>(bh) * p.S + qrow) * D;
 #pragma unroll 1
         for (int ch = 0; ch < D / 32; ++ch) {
-          uint32_t o[16];
-          tmem_ld_32x32b_x16(o_row + ch * 16, o);
+          uint32_t o[32];
+          tmem_ld_32x32b_x32(o_addr + ch * 32, o);
           tc_wait_ld();
           if (qrow < p.S) {
-            uint32_t hv[8];
+            uint32_t hv[16];
 #pragma unroll
-            for (int e = 0; e < 8; ++e)
+            for (int e = 0; e < 16; ++e)
               hv[e] = pack_half2(__uint_as_float(o[2 * e]) * inv_l, __uint_as_float(o[2 * e + 1]) * inv_l);
-            uint4* dst = reinterpret_cast<uint4*>(orow + ch * 16);
-            dst[0] = make_uint4(hv[0], hv[1], hv[2], hv[3]);
-            dst[1] = make_uint4(hv[4], hv[5], hv[6], hv[7]);
+            uint4* dst = reinterpret_cast<uint4*>(orow + ch * 32);
+#pragma unroll
+            for (int q4 = 0; q4 < 4; ++q4)
+              dst[q4] = make_uint4(hv[4 * q4], hv[4 * q4 + 1], hv[4 * q4 + 2], hv[4 * q4 + 3]);
           }
         }
       }
@@ -585,6 +517,15 @@ int launch_fa2(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& 
                                          Fa2Smem<D>::BYTES);
     if (e != cudaSuccess) return ntl_fail(NTL_ERR_CUDA, "cudaFuncSetAttribute(fa2): %s", cudaGetErrorString(e));
     done_mask.fetch_or(bit, std::memory_order_release);
+  }
+  {
+    // The in-kernel register split (8 warps x REGS_SOFTMAX + 4 warps x REGS_OTHER) must equal
+    // what the launch allocates (384 threads x REGS_LAUNCH), or the raising warps would wait
+    // for registers forever: refuse to launch a build whose register count differs.
+    cudaFuncAttributes fa;
+    if (cudaFuncGetAttributes(&fa, fa2_fwd_kernel<D>) != cudaSuccess || fa.numRegs != REGS_LAUNCH)
+      return ntl_fail(NTL_ERR_UNSUPPORTED, "attention: kernel compiled with %d registers, the split needs %d",
+                      fa.numRegs, REGS_LAUNCH);
   }
   dim3 grid(static_cast<unsigned>(p.n_qb), static_cast<unsigned>(heads), static_cast<unsigned>(batch));
   fa2_fwd_kernel<D><<<grid, THREADS, Fa2Smem<D>::BYTES, s>>>(mq, mk, mv, p);
