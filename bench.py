@@ -127,6 +127,78 @@ class RMSNormOp(RowOp):
         return n * (2 * rows * self.cols * 4 + self.cols * 4) / dt / 1e9, f"{n} x RMSNorm [{rows},{self.cols}]"
 
 
+class LayerNormOp(RowOp):
+    name = "layernorm"
+    rows, cols, eps = 4096, 1024, 1e-5
+    config = "LayerNorm X f32 [4096,1024] ~N(0,1), gamma f32 [1024] ~N(1,0.1), beta f32 [1024] ~N(0,0.1), eps 1e-5"
+
+    def setup(self):
+        from ntilang_b200 import kernels as K
+
+        self.kernel = K.layernorm(self.rows, self.cols, self.eps)
+        n = self.sets_needed(2 * self.rows * self.cols * 4)
+        self.sets = []
+        for s in range(n):
+            x = self.gen((self.rows, self.cols), 1.0, 1000 * self.rank + s)
+            w = self.gen((self.cols,), 0.1, 7 + s) + 1.0
+            b = self.gen((self.cols,), 0.1, 17 + s)
+            y = self.torch.empty_like(x)
+            self.sets.append(((x, w, b, y), (x, w, b), y))
+
+    def units(self):
+        return 2 * self.rows * self.cols * 4 + 2 * self.cols * 4
+
+    def cpu(self, seconds):
+        import numpy as np
+
+        from oracle import rowops
+
+        rows = 1024
+        x = np.random.default_rng(0).normal(size=(rows, self.cols)).astype(np.float32)
+        w = np.random.default_rng(1).normal(1, 0.1, size=self.cols).astype(np.float32)
+        b = np.random.default_rng(2).normal(0, 0.1, size=self.cols).astype(np.float32)
+        n, t0 = 0, time.perf_counter()
+        while time.perf_counter() - t0 < seconds:
+            rowops.layernorm(x, w, b, self.eps)
+            n += 1
+        dt = time.perf_counter() - t0
+        return n * (2 * rows * self.cols * 4 + 2 * self.cols * 4) / dt / 1e9, f"{n} x LayerNorm [{rows},{self.cols}]"
+
+
+class TransposeOp(RowOp):
+    name = "transpose"
+    m, n = 4096, 4096
+    config = "shared transpose A f32 [4096,4096] ~N(0,1) -> B [4096,4096] (README config)"
+
+    def setup(self):
+        from ntilang_b200 import kernels as K
+
+        self.kernel = K.transpose(self.m, self.n)
+        k = self.sets_needed(2 * self.m * self.n * 4)
+        self.sets = []
+        for s in range(k):
+            a = self.gen((self.m, self.n), 1.0, 1000 * self.rank + s)
+            b = self.torch.empty((self.n, self.m), device=self.device)
+            self.sets.append(((a, b), (a,), b))
+
+    def units(self):
+        return 2 * self.m * self.n * 4
+
+    def cpu(self, seconds):
+        import numpy as np
+
+        from oracle import rowops
+
+        m = 1024
+        a = np.random.default_rng(0).normal(size=(m, self.n)).astype(np.float32)
+        k, t0 = 0, time.perf_counter()
+        while time.perf_counter() - t0 < seconds:
+            rowops.transpose(a)
+            k += 1
+        dt = time.perf_counter() - t0
+        return k * 2 * m * self.n * 4 / dt / 1e9, f"{k} x transpose [{m},{self.n}]"
+
+
 class CumsumOp(RowOp):
     name = "cumsum"
     rows, cols = 32768, 256
@@ -345,7 +417,8 @@ class FA2CausalOp(FA2Op):
     config = "FlashAttention-2 fwd Q,K,V f16 [8,32,4096,128] ~N(0,1), scale 1/sqrt(128), causal"
 
 
-OPS = {c.name: c for c in (CumsumOp, RMSNormOp, SoftmaxOp, VaddOp, GemmOp, GemmBiasReluOp, FA2Op, FA2CausalOp)}
+OPS = {c.name: c for c in (CumsumOp, RMSNormOp, SoftmaxOp, VaddOp, GemmOp, GemmBiasReluOp, FA2Op, FA2CausalOp,
+                           LayerNormOp, TransposeOp)}
 
 
 # ------------------------------------------------------------------------------ clocks

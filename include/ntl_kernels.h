@@ -75,6 +75,17 @@ int ntl_softmax_f32(const float* x, float* y, int64_t rows, int64_t cols, ntl_st
 int ntl_rmsnorm_f32(const float* x, const float* w, float* y, int64_t rows, int64_t cols, float eps,
                     float inv_n, ntl_stream_t stream);
 
+/* LayerNorm y = ((x - mean) * rstd) * w + b over [rows, cols] fp32, w[cols], b[cols], with
+ * mean = sum(x) * inv_n and rstd = rsqrt(sum((x - mean)^2) * inv_n + eps), both sums the
+ * reference's balanced tree over the row padded to the next power of two.  Replaces the FFI
+ * call of the kernel emitted for examples/layernorm.py:18-43 (inv_n = 1/n at :10). */
+int ntl_layernorm_f32(const float* x, const float* w, const float* b, float* y, int64_t rows, int64_t cols,
+                      float eps, float inv_n, ntl_stream_t stream);
+
+/* b[n, m] = a[m, n]^T, fp32 row-major, out of place (bit-exact copy).  Replaces the FFI call
+ * of the shared-memory transpose emitted for examples/transpose.py:5-15. */
+int ntl_transpose_f32(const float* a, float* b, int64_t m, int64_t n, ntl_stream_t stream);
+
 /* Bias modes of ntl_gemm_f16_f32. */
 enum { NTL_BIAS_NONE = 0, NTL_BIAS_N = 1, NTL_BIAS_MN = 2, NTL_BIAS_M = 3 };
 

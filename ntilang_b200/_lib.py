@@ -28,6 +28,9 @@ SIGNATURES = {
     "ntl_softmax_f32": (ctypes.c_int, [c_f32p, c_f32p, c_i64, c_i64, ctypes.c_void_p]),
     "ntl_rmsnorm_f32": (ctypes.c_int, [c_f32p, c_f32p, c_f32p, c_i64, c_i64, ctypes.c_float, ctypes.c_float,
                                        ctypes.c_void_p]),
+    "ntl_layernorm_f32": (ctypes.c_int, [c_f32p, c_f32p, c_f32p, c_f32p, c_i64, c_i64, ctypes.c_float,
+                                         ctypes.c_float, ctypes.c_void_p]),
+    "ntl_transpose_f32": (ctypes.c_int, [c_f32p, c_f32p, c_i64, c_i64, ctypes.c_void_p]),
     "ntl_gemm_f16_f32": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, c_f32p, c_f32p, ctypes.c_int,
                                         ctypes.c_float, ctypes.c_int, c_i64, c_i64, c_i64, ctypes.c_int,
                                         ctypes.c_void_p]),

@@ -1,4 +1,4 @@
-// Row reductions: softmax and RMSNorm over [rows, cols] fp32.
+// Row reductions: softmax, RMSNorm and LayerNorm over [rows, cols] fp32.
 //
 // Reference (python/ntilang/codegen.py:1028-1240, examples/softmax.py:9-25,
 // examples/rmsnorm.py:13-37): the tile row is padded to P = next_pow2(cols) with the op's
@@ -25,6 +25,7 @@ constexpr unsigned kFull = 0xffffffffu;
 // shapes: softmax 16384x512 is fastest with 8, RMSNorm 4096x1024 with 16 (6.4 vs 6.8 us).
 constexpr int kSoftmaxWarpsPerBlock = 8;
 constexpr int kRmsnormWarpsPerBlock = 16;
+constexpr int kLayernormWarpsPerBlock = 16;
 
 template <bool VEC>
 __device__ __forceinline__ void load4(const float* __restrict__ row, int64_t col, int64_t cols, float pad,
@@ -266,6 +267,131 @@ __global__ void __launch_bounds__(256) rmsnorm_rows_cta(const float* __restrict_
   }
 }
 
+// ----------------------------------------------------------------------- LayerNorm
+//
+// examples/layernorm.py:18-43: mean = tree_sum(x) * inv_n; d = x - mean (0 in the padding);
+// rstd = rsqrt(tree_sum(d * d) * inv_n + eps); y = ((d * rstd) * w) + b, every step rounded
+// separately (no fused multiply-add), both sums perfect trees over the padded row.
+
+template <int NCH>
+__device__ __forceinline__ void centre(float (&v)[NCH][4], float mean, int64_t col0, int64_t stride, int64_t cols) {
+#pragma unroll
+  for (int c = 0; c < NCH; ++c)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const int64_t col = col0 + static_cast<int64_t>(c) * stride + e;
+      v[c][e] = col < cols ? __fsub_rn(v[c][e], mean) : 0.0f;
+    }
+}
+
+template <int NCH, bool VEC>
+__global__ void __launch_bounds__(kLayernormWarpsPerBlock * 32) layernorm_rows_warp(const float* __restrict__ x,
+                                                                                    const float* __restrict__ w,
+                                                                                    const float* __restrict__ b,
+                                                                                    float* __restrict__ y,
+                                                                                    int64_t rows, int64_t cols,
+                                                                                    float eps, float inv_n) {
+  const int lane = threadIdx.x & 31;
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * kLayernormWarpsPerBlock + (threadIdx.x >> 5);
+  if (lane == 0 && row < rows) prefetch_l2(x + row * cols, cols * 4);
+  if (threadIdx.x == 32) prefetch_l2(w, cols * 4);
+  if (threadIdx.x == 64) prefetch_l2(b, cols * 4);
+  pdl_wait();
+  pdl_trigger();
+  if (row >= rows) return;
+  const float* xr = x + row * cols;
+  float* yr = y + row * cols;
+  float v[NCH][4];
+#pragma unroll
+  for (int c = 0; c < NCH; ++c) load4<VEC>(xr, static_cast<int64_t>(c) * 128 + lane * 4, cols, 0.0f, v[c]);
+  float s[NCH];
+#pragma unroll
+  for (int c = 0; c < NCH; ++c) s[c] = warp_tree_sum(lane_pair_sum(v[c]));
+  const float mean = __fmul_rn(chunk_tree<NCH>(s), inv_n);
+  centre<NCH>(v, mean, lane * 4, 128, cols);
+#pragma unroll
+  for (int c = 0; c < NCH; ++c) {
+    float q[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) q[e] = __fmul_rn(v[c][e], v[c][e]);
+    s[c] = warp_tree_sum(lane_pair_sum(q));
+  }
+  const float rstd = rsqrtf(__fadd_rn(__fmul_rn(chunk_tree<NCH>(s), inv_n), eps));
+#pragma unroll
+  for (int c = 0; c < NCH; ++c) {
+    const int64_t col = static_cast<int64_t>(c) * 128 + lane * 4;
+    float wv[4], bv[4];
+    load_w4<VEC>(w, col, cols, wv);
+    load_w4<VEC>(b, col, cols, bv);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) v[c][e] = __fadd_rn(__fmul_rn(__fmul_rn(v[c][e], rstd), wv[e]), bv[e]);
+    store4<VEC>(yr, col, cols, v[c]);
+  }
+}
+
+// One CTA (8 warps) per row; position bits (element 2, lane 5, warp 3, chunk).
+template <int NCH>
+__device__ __forceinline__ float cta_tree_sum(float (&part)[NCH], float (*red)[8], int lane, int warp) {
+#pragma unroll
+  for (int c = 0; c < NCH; ++c) {
+    const float t = warp_tree_sum(part[c]);
+    if (lane == 0) red[c][warp] = t;
+  }
+  __syncthreads();
+  float s[NCH];
+#pragma unroll
+  for (int c = 0; c < NCH; ++c) {
+    float t[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) t[k] = red[c][k];
+    s[c] = chunk_tree<8>(t);
+  }
+  __syncthreads();  // red is reused by the next sum
+  return chunk_tree<NCH>(s);
+}
+
+template <int NCH, bool VEC>
+__global__ void __launch_bounds__(256) layernorm_rows_cta(const float* __restrict__ x, const float* __restrict__ w,
+                                                          const float* __restrict__ b, float* __restrict__ y,
+                                                          int64_t rows, int64_t cols, float eps, float inv_n) {
+  __shared__ float red[NCH][8];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int64_t row = blockIdx.x;
+  if (threadIdx.x == 0) prefetch_l2(x + row * cols, cols < 4096 ? cols * 4 : 16384);  // first 16 KB
+  if (threadIdx.x == 32) prefetch_l2(w, cols * 4);
+  if (threadIdx.x == 64) prefetch_l2(b, cols * 4);
+  pdl_wait();
+  pdl_trigger();
+  const float* xr = x + row * cols;
+  float* yr = y + row * cols;
+  float v[NCH][4];
+#pragma unroll
+  for (int c = 0; c < NCH; ++c) load4<VEC>(xr, static_cast<int64_t>(c) * 1024 + threadIdx.x * 4, cols, 0.0f, v[c]);
+  float part[NCH];
+#pragma unroll
+  for (int c = 0; c < NCH; ++c) part[c] = lane_pair_sum(v[c]);
+  const float mean = __fmul_rn(cta_tree_sum<NCH>(part, red, lane, warp), inv_n);
+  centre<NCH>(v, mean, threadIdx.x * 4, 1024, cols);
+#pragma unroll
+  for (int c = 0; c < NCH; ++c) {
+    float q[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) q[e] = __fmul_rn(v[c][e], v[c][e]);
+    part[c] = lane_pair_sum(q);
+  }
+  const float rstd = rsqrtf(__fadd_rn(__fmul_rn(cta_tree_sum<NCH>(part, red, lane, warp), inv_n), eps));
+#pragma unroll
+  for (int c = 0; c < NCH; ++c) {
+    const int64_t col = static_cast<int64_t>(c) * 1024 + threadIdx.x * 4;
+    float wv[4], bv[4];
+    load_w4<VEC>(w, col, cols, wv);
+    load_w4<VEC>(b, col, cols, bv);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) v[c][e] = __fadd_rn(__fmul_rn(__fmul_rn(v[c][e], rstd), wv[e]), bv[e]);
+    store4<VEC>(yr, col, cols, v[c]);
+  }
+}
+
 // --------------------------------------------------------------------- dispatch
 
 constexpr int64_t kMaxWarpCols = 2048;   // 16 chunks of 128 per warp
@@ -280,20 +406,20 @@ struct Dispatch;
     if (cols <= kMaxWarpCols) {                                                                         \
       const int64_t blocks = (rows + (WPB)-1) / (WPB);                                                  \
       NTL_REQUIRE(blocks <= 0x7fffffff, NTL_ERR_UNSUPPORTED, "too many rows");                         \
-      dim3 g(static_cast<unsigned>(blocks)), b((WPB)*32);                                               \
-      if (nch <= 1) ntl_launch_pdl(KW<1, VEC>, g, b, 0, s, __VA_ARGS__);                                \
-      else if (nch <= 2) ntl_launch_pdl(KW<2, VEC>, g, b, 0, s, __VA_ARGS__);                           \
-      else if (nch <= 4) ntl_launch_pdl(KW<4, VEC>, g, b, 0, s, __VA_ARGS__);                           \
-      else if (nch <= 8) ntl_launch_pdl(KW<8, VEC>, g, b, 0, s, __VA_ARGS__);                           \
-      else ntl_launch_pdl(KW<16, VEC>, g, b, 0, s, __VA_ARGS__);                                        \
+      dim3 ntl_grid_(static_cast<unsigned>(blocks)), ntl_block_((WPB)*32);                                               \
+      if (nch <= 1) ntl_launch_pdl(KW<1, VEC>, ntl_grid_, ntl_block_, 0, s, __VA_ARGS__);                                \
+      else if (nch <= 2) ntl_launch_pdl(KW<2, VEC>, ntl_grid_, ntl_block_, 0, s, __VA_ARGS__);                           \
+      else if (nch <= 4) ntl_launch_pdl(KW<4, VEC>, ntl_grid_, ntl_block_, 0, s, __VA_ARGS__);                           \
+      else if (nch <= 8) ntl_launch_pdl(KW<8, VEC>, ntl_grid_, ntl_block_, 0, s, __VA_ARGS__);                           \
+      else ntl_launch_pdl(KW<16, VEC>, ntl_grid_, ntl_block_, 0, s, __VA_ARGS__);                                        \
     } else {                                                                                            \
       NTL_REQUIRE(rows <= 0x7fffffff, NTL_ERR_UNSUPPORTED, "too many rows");                           \
       const int64_t cch = (cols + 1023) / 1024;                                                         \
-      dim3 g(static_cast<unsigned>(rows)), b(256);                                                      \
-      if (cch <= 2) ntl_launch_pdl(KC<2, VEC>, g, b, 0, s, __VA_ARGS__);                                \
-      else if (cch <= 4) ntl_launch_pdl(KC<4, VEC>, g, b, 0, s, __VA_ARGS__);                           \
-      else if (cch <= 8) ntl_launch_pdl(KC<8, VEC>, g, b, 0, s, __VA_ARGS__);                           \
-      else ntl_launch_pdl(KC<16, VEC>, g, b, 0, s, __VA_ARGS__);                                        \
+      dim3 ntl_grid_(static_cast<unsigned>(rows)), ntl_block_(256);                                                      \
+      if (cch <= 2) ntl_launch_pdl(KC<2, VEC>, ntl_grid_, ntl_block_, 0, s, __VA_ARGS__);                                \
+      else if (cch <= 4) ntl_launch_pdl(KC<4, VEC>, ntl_grid_, ntl_block_, 0, s, __VA_ARGS__);                           \
+      else if (cch <= 8) ntl_launch_pdl(KC<8, VEC>, ntl_grid_, ntl_block_, 0, s, __VA_ARGS__);                           \
+      else ntl_launch_pdl(KC<16, VEC>, ntl_grid_, ntl_block_, 0, s, __VA_ARGS__);                                        \
     }                                                                                                   \
   } while (0)
 
@@ -330,4 +456,24 @@ extern "C" int ntl_rmsnorm_f32(const float* x, const float* w, float* y, int64_t
     NTL_ROW_DISPATCH(rmsnorm_rows_warp, rmsnorm_rows_cta, false, kRmsnormWarpsPerBlock, x, w, y, rows, cols, eps, inv_n);
   ntl_note_launch();
   return ntl_check_launch("rmsnorm launch");
+}
+
+extern "C" int ntl_layernorm_f32(const float* x, const float* w, const float* b, float* y, int64_t rows,
+                                 int64_t cols, float eps, float inv_n, ntl_stream_t stream) {
+  NTL_REQUIRE(rows >= 0 && cols >= 0, NTL_ERR_INVALID, "layernorm: negative size");
+  if (rows == 0 || cols == 0) return NTL_OK;
+  NTL_REQUIRE(x && w && b && y, NTL_ERR_INVALID, "layernorm: NULL pointer");
+  NTL_REQUIRE(cols <= kMaxCtaCols, NTL_ERR_UNSUPPORTED, "layernorm: rows longer than %lld columns are not supported",
+              (long long)kMaxCtaCols);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const bool vec = (cols % 4 == 0) && ntl_aligned(x, 16) && ntl_aligned(y, 16) && ntl_aligned(w, 16) &&
+                   ntl_aligned(b, 16);
+  if (vec)
+    NTL_ROW_DISPATCH(layernorm_rows_warp, layernorm_rows_cta, true, kLayernormWarpsPerBlock, x, w, b, y, rows, cols,
+                     eps, inv_n);
+  else
+    NTL_ROW_DISPATCH(layernorm_rows_warp, layernorm_rows_cta, false, kLayernormWarpsPerBlock, x, w, b, y, rows,
+                     cols, eps, inv_n);
+  ntl_note_launch();
+  return ntl_check_launch("layernorm launch");
 }

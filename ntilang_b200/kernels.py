@@ -4,7 +4,7 @@ Each factory returns a TileLang program; ``jit`` reads it, recognises the family
 returns a cached ``CompiledKernel`` whose call allocates the last parameter as the
 output, e.g. ``y = softmax(16384, 512)(x)``.  The programs follow the operator semantics
 of the reference's examples (vector_add.py, cumsum.py, softmax.py, rmsnorm.py,
-matmul.py, matmul_relu.py, flash_attention.py); the tile sizes written in them are
+layernorm.py, transpose.py, matmul.py, matmul_relu.py, flash_attention.py); the tile sizes written in them are
 program-level hints only — the sm_100a kernels choose their own tiles.
 """
 
@@ -88,6 +88,56 @@ def rmsnorm(rows, cols, eps=1e-6, rows_per_block=4):
                     Y[b * rows_per_block + r, c] = xs[r, c] * rinv[r] * G[c]
 
     return row_rmsnorm
+
+
+@jit(out_idx=[-1])
+def layernorm(rows, cols, eps=1e-5, rows_per_block=4):
+    width = 1 << max(0, (cols - 1).bit_length())
+    scale = 1.0 / cols
+
+    @T.prim_func
+    def row_layernorm(X: T.Tensor((rows, cols), "float32"), G: T.Tensor((cols,), "float32"),
+                      Bb: T.Tensor((cols,), "float32"), Y: T.Tensor((rows, cols), "float32")):
+        with T.Kernel(T.ceildiv(rows, rows_per_block), threads=128) as b:
+            xs = T.alloc_fragment((rows_per_block, width), "float32")
+            sq = T.alloc_fragment((rows_per_block, width), "float32")
+            acc = T.alloc_fragment((rows_per_block,), "float32")
+            var = T.alloc_fragment((rows_per_block,), "float32")
+            mean = T.alloc_fragment((rows_per_block,), "float32")
+            rstd = T.alloc_fragment((rows_per_block,), "float32")
+            for r, c in T.Parallel(rows_per_block, width):
+                xs[r, c] = X[b * rows_per_block + r, c] if c < cols else 0.0
+            T.reduce_sum(xs, acc, dim=1)
+            for r in T.Parallel(rows_per_block):
+                mean[r] = acc[r] * scale
+            for r, c in T.Parallel(rows_per_block, width):
+                if c < cols:
+                    d = xs[r, c] - mean[r]
+                    sq[r, c] = d * d
+                else:
+                    sq[r, c] = 0.0
+            T.reduce_sum(sq, var, dim=1)
+            for r in T.Parallel(rows_per_block):
+                rstd[r] = T.rsqrt(var[r] * scale + eps)
+            for r, c in T.Parallel(rows_per_block, width):
+                if c < cols:
+                    Y[b * rows_per_block + r, c] = (xs[r, c] - mean[r]) * rstd[r] * G[c] + Bb[c]
+
+    return row_layernorm
+
+
+@jit(out_idx=[-1])
+def transpose(m, n, tile=32):
+    @T.prim_func
+    def shared_transpose(A: T.Tensor((m, n), "float32"), B: T.Tensor((n, m), "float32")):
+        with T.Kernel(T.ceildiv(m, tile), T.ceildiv(n, tile), threads=128) as (bx, by):
+            t = T.alloc_shared((tile, tile), "float32")
+            for i, j in T.Parallel(tile, tile):
+                T.copy(A[bx * tile + i, by * tile + j], t[i, j])
+            for i, j in T.Parallel(tile, tile):
+                B[by * tile + i, bx * tile + j] = t[j, i]
+
+    return shared_transpose
 
 
 def _gemm_program(m, n, k, bm, bn, bk, stages, epilogue, trans_b=False):
@@ -232,5 +282,5 @@ def flash_attention(batch, heads, seq_len, dim, is_causal=False, block_m=128, bl
     return attention
 
 
-__all__ = ["cumsum", "flash_attention", "matmul", "matmul_bias_relu", "matmul_scaled_bias_relu", "rmsnorm",
-           "softmax", "vector_add"]
+__all__ = ["cumsum", "flash_attention", "layernorm", "matmul", "matmul_bias_relu", "matmul_scaled_bias_relu", "rmsnorm",
+           "softmax", "transpose", "vector_add"]

@@ -64,14 +64,21 @@ def launch(spec: OpSpec, tensors, stream: int) -> None:
         x, w, y = tensors[a["x"]], tensors[a["w"]], tensors[a["y"]]
         _lib.call("ntl_rmsnorm_f32", _ptr(x), _ptr(w), _ptr(y), int(x.shape[0]), int(x.shape[1]),
                   float(p["eps"]), float(p["inv_n"]), stream)
+    elif f == "layernorm":
+        x, w, b, y = tensors[a["x"]], tensors[a["w"]], tensors[a["b"]], tensors[a["y"]]
+        _lib.call("ntl_layernorm_f32", _ptr(x), _ptr(w), _ptr(b), _ptr(y), int(x.shape[0]), int(x.shape[1]),
+                  float(p["eps"]), float(p["inv_n"]), stream)
+    elif f == "transpose":
+        src, dst = tensors[a["a"]], tensors[a["b"]]
+        _lib.call("ntl_transpose_f32", _ptr(src), _ptr(dst), int(src.shape[0]), int(src.shape[1]), stream)
     elif f == "gemm":
         A, B, C = tensors[a["a"]], tensors[a["b"]], tensors[a["c"]]
         bias = tensors[a["bias"]] if "bias" in a else None
         M, K = int(A.shape[0]), int(A.shape[1])
         N = int(B.shape[0]) if p["transpose_b"] else int(B.shape[1])
-        # Data-parallel tiles: on B200 the stream-K split of the last wave (ntl_gemm_f16_f32_ws)
-        # measured slower for every shape tried (the mainloop is bound by L2->SM bandwidth,
-        # which stream-K spreads over more SMs without reducing).
+        # Data-parallel tiles: on B200 splitting the last wave along K (ntl_gemm_f16_f32_ws)
+        # measured no faster at any shape tried; the partial-sum fixup costs about what the
+        # idle part of the wave does.
         _lib.call("ntl_gemm_f16_f32", _ptr(A), _ptr(B), _ptr(C), _ptr(bias) if bias is not None else None,
                   int(p["bias_mode"]), float(p["alpha"]), int(p["relu"]), M, N, K, int(p["transpose_b"]), stream)
     elif f == "fa2":
@@ -88,6 +95,8 @@ ABI_CALL = {
     "cumsum": "ntl_cumsum_f32(X, Y, rows, cols, reverse, stream)",
     "softmax": "ntl_softmax_f32(X, Y, rows, cols, stream)",
     "rmsnorm": "ntl_rmsnorm_f32(X, W, Y, rows, cols, eps, inv_n, stream)",
+    "layernorm": "ntl_layernorm_f32(X, W, B, Y, rows, cols, eps, inv_n, stream)",
+    "transpose": "ntl_transpose_f32(A, B, m, n, stream)",
     "gemm": "ntl_gemm_f16_f32(A, B, C, bias, bias_mode, alpha, relu, M, N, K, b_trans, stream)",
     "fa2": "ntl_fa2_fwd_f16(Q, K, V, O, batch, heads, seq, dim, scale_log2, causal, stream)",
 }

@@ -434,6 +434,111 @@ def _match_rmsnorm(prog: Program) -> OpSpec:
                   {"x": _param_index(prog, xs.name), "w": _param_index(prog, w.name), "y": _param_index(prog, out_name)})
 
 
+def _mean_of(e, cols):
+    """``Red(sum, row) * inv_n`` (or ``/ n``) -> (row, inv_n)."""
+    need(isinstance(e, Bin) and e.op in ("*", "/"), "mean = sum * inv_n")
+    red, scale = e.a, e.b
+    if isinstance(red, Const) and e.op == "*":
+        red, scale = scale, red
+    need(isinstance(scale, Const), "mean scale is a constant")
+    need(isinstance(red, Red) and red.kind == "sum", "mean of a row sum")
+    inv_n = float(scale.value) if e.op == "*" else 1.0 / float(scale.value)
+    return _strip_pad(red.expr, cols, 0.0), inv_n
+
+
+def _match_layernorm(prog: Program) -> OpSpec:
+    """examples/layernorm.py:18-43: y = ((x - mean) * rstd) * w + b, mean = sum(x) * (1/n),
+    rstd = rsqrt(sum((x - mean)^2) * (1/n) + eps); padded columns contribute 0 to both sums."""
+    ev = RowEval(prog)
+    ev.run(prog.body)
+    need(len(ev.out) == 1, "layernorm writes one output")
+    (out_name, y), = ev.out.items()
+    y = _fold(y)
+    need(isinstance(y, Bin) and y.op == "+", "layernorm output is (...) * w + b")
+    scaled, b = y.a, y.b
+    if isinstance(scaled, W):
+        scaled, b = b, scaled
+    need(isinstance(b, W), "shift is a 1-D parameter")
+    need(isinstance(scaled, Bin) and scaled.op == "*", "((x - mean) * rstd) * w")
+    norm, w = scaled.a, scaled.b
+    if isinstance(norm, W):
+        norm, w = w, norm
+    need(isinstance(w, W), "scale is a 1-D parameter")
+    need(isinstance(norm, Bin) and norm.op == "*", "(x - mean) * rstd")
+    centred, rstd = norm.a, norm.b
+    if isinstance(centred, Call):
+        centred, rstd = rstd, centred
+    need(isinstance(centred, Bin) and centred.op == "-", "x - mean")
+    xs = _strip_pad(centred.a, ev.cols, 0.0)
+    need(isinstance(xs, X), "normalised value is an input row")
+    row, inv_n = _mean_of(centred.b, ev.cols)
+    need(row == xs, "mean of the same input row")
+    need(isinstance(rstd, Call) and rstd.fn == "rsqrt", "rstd uses rsqrt")
+    arg = rstd.args[0]
+    need(isinstance(arg, Bin) and arg.op == "+", "rsqrt(var + eps)")
+    var, eps = arg.a, arg.b
+    if isinstance(var, Const):
+        var, eps = eps, var
+    need(isinstance(eps, Const), "eps is a constant")
+    sq, inv_n2 = _mean_of(var, ev.cols)
+    need(inv_n2 == inv_n, "mean and variance use the same 1/n")
+    need(isinstance(sq, Bin) and sq.op == "*" and sq.a == sq.b, "variance of a square")
+    d = sq.a
+    need(isinstance(d, Bin) and d.op == "-" and _strip_pad(d.a, ev.cols, 0.0) == xs
+         and _mean_of(d.b, ev.cols) == (xs, inv_n), "squares of x - mean")
+    shape = prog.buffers[xs.name].shape
+    need(prog.buffers[out_name].shape == shape, "input and output shapes match")
+    need(prog.buffers[w.name].shape == (shape[1],) and prog.buffers[b.name].shape == (shape[1],),
+         "weight and bias lengths equal the row length")
+    need(xs.name != out_name, "in-place layernorm is not supported")
+    need(_covers(prog, ev.bx, ev.rb, shape[0]), "grid must cover every row")
+    need(all(prog.buffers[n].dtype == "float32" for n in (xs.name, w.name, b.name, out_name)),
+         "layernorm kernels are float32")
+    return OpSpec("layernorm", {"rows": _dim(shape[0]), "cols": ev.cols, "eps": float(eps.value), "inv_n": inv_n},
+                  {"x": _param_index(prog, xs.name), "w": _param_index(prog, w.name), "b": _param_index(prog, b.name),
+                   "y": _param_index(prog, out_name)})
+
+
+# ------------------------------------------------------------------------------ transpose
+
+
+def _match_transpose(prog: Program) -> OpSpec:
+    """examples/transpose.py:5-15: B[by*T + i, bx*T + j] = tile[j, i] after
+    tile[i, j] = A[bx*T + i, by*T + j], i.e. B = A^T (out-of-range elements untouched)."""
+    need(len(prog.grid) == 2, "transpose uses a 2-D grid")
+    bx, by = prog.block_vars
+    body = _body(prog.body)
+    need(len(body) == 2 and all(isinstance(s, Parallel) for s in body), "two T.Parallel loops")
+    load, store = body
+    need(len(load.vars) == 2 and len(store.vars) == 2 and load.extents == store.extents
+         and load.extents[0] == load.extents[1], "square tile loops")
+    t = load.extents[0]
+    need(len(load.body) == 1 and len(store.body) == 1, "one statement per loop")
+    li, lj = load.vars
+    st0 = load.body[0]
+    if isinstance(st0, Copy):
+        need(st0.src.point and st0.dst.point, "element copies")
+        src_buf, src_idx, tile, tile_idx = st0.src.buf, st0.src.starts, st0.dst.buf, st0.dst.starts
+    else:
+        need(isinstance(st0, Store) and isinstance(st0.value, Load), "tile[i, j] = A[...]")
+        src_buf, src_idx, tile, tile_idx = st0.value.buf, st0.value.idx, st0.buf, st0.idx
+    need(prog.buffers[tile].scope in ("shared", "fragment") and prog.buffers[tile].shape == (t, t), "a T x T tile")
+    need(_aff_is(tile_idx[0], {li: 1}) and _aff_is(tile_idx[1], {lj: 1}), "tile written at [i, j]")
+    need(_aff_is(src_idx[0], {bx: t, li: 1}) and _aff_is(src_idx[1], {by: t, lj: 1}), "A read at [bx*T + i, by*T + j]")
+    si, sj = store.vars
+    st1 = store.body[0]
+    need(isinstance(st1, Store) and isinstance(st1.value, Load) and st1.value.buf == tile, "B[...] = tile[j, i]")
+    need(_aff_is(st1.value.idx[0], {sj: 1}) and _aff_is(st1.value.idx[1], {si: 1}), "tile read at [j, i]")
+    need(_aff_is(st1.idx[0], {by: t, si: 1}) and _aff_is(st1.idx[1], {bx: t, sj: 1}), "B written at [by*T + i, bx*T + j]")
+    a, b = src_buf, st1.buf
+    need(_is_param(prog, a) and _is_param(prog, b) and a != b, "distinct parameters A and B")
+    m, n = prog.buffers[a].shape
+    need(prog.buffers[b].shape == (n, m), "B has the transposed shape")
+    need(_covers(prog, bx, t, m) and _covers(prog, by, t, n), "grid must cover A")
+    need(prog.buffers[a].dtype == "float32" and prog.buffers[b].dtype == "float32", "transpose kernels are float32")
+    return OpSpec("transpose", {"m": _dim(m), "n": _dim(n)}, {"a": _param_index(prog, a), "b": _param_index(prog, b)})
+
+
 # ----------------------------------------------------------------------------- elementwise
 
 
@@ -827,6 +932,8 @@ MATCHERS = (
     ("cumsum", _match_cumsum),
     ("softmax", _match_softmax),
     ("rmsnorm", _match_rmsnorm),
+    ("layernorm", _match_layernorm),
+    ("transpose", _match_transpose),
     ("elementwise", _match_elementwise),
 )
 
@@ -844,7 +951,7 @@ def recognize(prog: Program) -> OpSpec:
             reasons.append(f"{name}: {type(exc).__name__} {exc}")
     raise CompileError(
         f"{prog.name}: program is not one of the op families implemented by the sm_100a kernels "
-        "(elementwise, cumsum, softmax, rmsnorm, gemm, fa2):\n  " + "\n  ".join(reasons)
+        "(elementwise, cumsum, softmax, rmsnorm, layernorm, transpose, gemm, fa2):\n  " + "\n  ".join(reasons)
     )
 
 

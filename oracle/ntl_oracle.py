@@ -109,6 +109,28 @@ def rmsnorm_rows(x: np.ndarray, w: np.ndarray, eps: float, inv_n: float | None =
     return ((x * inv[..., None]).astype(np.float32) * w).astype(np.float32)
 
 
+def layernorm_rows(x: np.ndarray, w: np.ndarray, b: np.ndarray, eps: float,
+                   inv_n: float | None = None) -> np.ndarray:
+    """examples/layernorm.py:18-43 in the reference's order, every step rounded to float32:
+    mean = tree_sum(x) * inv_n; d = x - mean; rstd = 1 / sqrt(tree_sum(d * d) * inv_n + eps)
+    (the evaluator's rsqrt, testing.py:98); y = ((d * rstd) * w) + b."""
+    x = np.asarray(x, dtype=np.float32)
+    w = np.asarray(w, dtype=np.float32)
+    b = np.asarray(b, dtype=np.float32)
+    n = x.shape[-1]
+    inv_n = np.float32(1.0 / n if inv_n is None else inv_n)
+    mean = (tree_sum_rows(x) * inv_n).astype(np.float32)
+    d = (x - mean[..., None]).astype(np.float32)
+    var = (tree_sum_rows((d * d).astype(np.float32)) * inv_n).astype(np.float32)
+    rstd = (np.float32(1.0) / np.sqrt((var + np.float32(eps)).astype(np.float32))).astype(np.float32)
+    return ((((d * rstd[..., None]).astype(np.float32)) * w).astype(np.float32) + b).astype(np.float32)
+
+
+def transpose(a: np.ndarray) -> np.ndarray:
+    """examples/transpose.py:5-15: B = A^T (an exact copy)."""
+    return np.ascontiguousarray(np.asarray(a).T)
+
+
 # -------------------------------------------------------------------------------- GEMM
 
 BIAS_NONE, BIAS_N, BIAS_MN, BIAS_M = 0, 1, 2, 3

@@ -14,6 +14,7 @@
  *   rmsnorm: examples/rmsnorm.py:13-37 — tree sum of squares, 1/sqrtf(ss*inv_n + eps),
  *            (x * inv) * w.
  *   vadd   : examples/vector_add.py:5-10.
+ *   layernorm: examples/layernorm.py:18-43.  transpose: examples/transpose.py:5-15.
  */
 #include <math.h>
 #include <pthread.h>
@@ -178,4 +179,57 @@ void oracle_rmsnorm_f32(const float* x, const float* w, float* y, int64_t rows, 
                         float inv_n) {
   struct row_ctx c = {x, w, y, cols, 0, eps, inv_n};
   parallel_for(rows, rmsnorm_range, &c);
+}
+
+/* examples/layernorm.py:18-43: mean = tree(x) * inv_n; d = x - mean; rstd = 1 / sqrtf(tree(d*d)
+ * * inv_n + eps) (the reference evaluator's rsqrt, testing.py:98); y = ((d * rstd) * w) + b. */
+struct ln_ctx {
+  const float *x, *w, *b;
+  float* y;
+  int64_t cols;
+  float eps, inv_n;
+};
+
+static void layernorm_range(void* p, int64_t b, int64_t e) {
+  struct ln_ctx* c = (struct ln_ctx*)p;
+  const int64_t cols = c->cols, pw = next_pow2(cols);
+  float* work = (float*)malloc((size_t)pw * sizeof(float));
+  for (int64_t r = b; r < e; ++r) {
+    const float* xr = c->x + r * cols;
+    float* yr = c->y + r * cols;
+    for (int64_t j = 0; j < pw; ++j) work[j] = j < cols ? xr[j] : 0.0f;
+    const float mean = tree_sum(work, pw) * c->inv_n;
+    for (int64_t j = 0; j < pw; ++j) {
+      const float d = j < cols ? xr[j] - mean : 0.0f;
+      work[j] = d * d;
+    }
+    const float var = tree_sum(work, pw) * c->inv_n;
+    const float rstd = 1.0f / sqrtf(var + c->eps);
+    for (int64_t j = 0; j < cols; ++j) yr[j] = ((xr[j] - mean) * rstd) * c->w[j] + c->b[j];
+  }
+  free(work);
+}
+
+void oracle_layernorm_f32(const float* x, const float* w, const float* b, float* y, int64_t rows, int64_t cols,
+                          float eps, float inv_n) {
+  struct ln_ctx c = {x, w, b, y, cols, eps, inv_n};
+  parallel_for(rows, layernorm_range, &c);
+}
+
+struct tr_ctx {
+  const float* a;
+  float* b;
+  int64_t m, n;
+};
+
+static void transpose_range(void* p, int64_t b, int64_t e) {
+  struct tr_ctx* c = (struct tr_ctx*)p;
+  for (int64_t r = b; r < e; ++r)
+    for (int64_t j = 0; j < c->n; ++j) c->b[j * c->m + r] = c->a[r * c->n + j];
+}
+
+/* examples/transpose.py:5-15: b[n, m] = a[m, n]^T. */
+void oracle_transpose_f32(const float* a, float* b, int64_t m, int64_t n) {
+  struct tr_ctx c = {a, b, m, n};
+  parallel_for(m, transpose_range, &c);
 }

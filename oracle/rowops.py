@@ -34,6 +34,8 @@ def lib():
         h.oracle_cumsum_f32.argtypes = [p, p, i64, i64, ctypes.c_int]
         h.oracle_softmax_f32.argtypes = [p, p, i64, i64]
         h.oracle_rmsnorm_f32.argtypes = [p, p, p, i64, i64, ctypes.c_float, ctypes.c_float]
+        h.oracle_layernorm_f32.argtypes = [p, p, p, p, i64, i64, ctypes.c_float, ctypes.c_float]
+        h.oracle_transpose_f32.argtypes = [p, p, i64, i64]
         _lib = h
     return _lib
 
@@ -80,3 +82,21 @@ def rmsnorm(x, w, eps, inv_n=None):
     inv_n = 1.0 / cols if inv_n is None else inv_n
     lib().oracle_rmsnorm_f32(x.ctypes.data, w.ctypes.data, y.ctypes.data, x.size // cols, cols, eps, inv_n)
     return y
+
+
+def layernorm(x, w, b, eps, inv_n=None):
+    x, w, b = _f32(x), _f32(w), _f32(b)
+    y = np.empty_like(x)
+    cols = x.shape[-1]
+    inv_n = 1.0 / cols if inv_n is None else inv_n
+    lib().oracle_layernorm_f32(x.ctypes.data, w.ctypes.data, b.ctypes.data, y.ctypes.data, x.size // cols, cols, eps,
+                               inv_n)
+    return y
+
+
+def transpose(a):
+    a = _f32(a)
+    m, n = a.shape
+    b = np.empty((n, m), dtype=np.float32)
+    lib().oracle_transpose_f32(a.ctypes.data, b.ctypes.data, m, n)
+    return b

@@ -36,7 +36,9 @@ def load_example(ref: Path, name: str):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", required=True, type=Path)
+    ap.add_argument("--only", default="", help="comma-separated case-name prefixes to (re)write")
     args = ap.parse_args()
+    only = tuple(x for x in args.only.split(",") if x)
     ref = args.reference.resolve()
     # The reference package is also called `ntilang`: make sure it, not this repo's alias, is imported.
     sys.path = [str(ref / "python")] + [p for p in sys.path if Path(p or ".").resolve() != HERE.parents[1]]
@@ -46,7 +48,12 @@ def main():
 
     assert Path(ntilang.__file__).resolve().is_relative_to(ref), ntilang.__file__
 
+    def wanted(name):
+        return not only or name.startswith(only)
+
     def save(name, **arrays):
+        if not wanted(name):
+            return
         np.savez_compressed(HERE / f"{name}.npz", **arrays)
         print("wrote", name, {k: getattr(v, "shape", v) for k, v in arrays.items()})
 
@@ -105,6 +112,30 @@ def main():
         y = np.full_like(x, np.nan)
         reference(rn.rmsnorm(rows, cols, eps=1e-6), x, w, y)
         save(f"rmsnorm_{rows}x{cols}", x=x, w=w, y=y, eps=np.array(1e-6))
+
+    # LayerNorm (examples/layernorm.py)
+    ln = load_example(ref, "layernorm")
+    for rows, cols, seed in ((6, 1024, 7), (5, 768, 8), (3, 100, 9)):
+        if not wanted(f"layernorm_{rows}x{cols}"):
+            continue
+        rng = np.random.default_rng(seed)
+        x = (rng.normal(size=(rows, cols)) * 2.0 + 0.5).astype(np.float32)
+        w = rng.normal(1.0, 0.1, size=cols).astype(np.float32)
+        bb = rng.normal(0.0, 0.1, size=cols).astype(np.float32)
+        y = np.full_like(x, np.nan)
+        reference(ln.layernorm(rows, cols, eps=1e-5), x, w, bb, y)
+        save(f"layernorm_{rows}x{cols}", x=x, w=w, b=bb, y=y, eps=np.array(1e-5))
+
+    # Shared-memory transpose (examples/transpose.py)
+    tr = load_example(ref, "transpose")
+    for m, n, seed in ((65, 71, 10), (33, 130, 11)):
+        if not wanted(f"transpose_{m}x{n}"):
+            continue
+        rng = np.random.default_rng(seed)
+        a = rng.normal(size=(m, n)).astype(np.float32)
+        bt = np.full((n, m), np.nan, np.float32)
+        reference(tr.transpose(m, n), a, bt)
+        save(f"transpose_{m}x{n}", a=a, b=bt)
 
     # GEMM (examples/matmul.py) and GEMM + bias + ReLU (examples/matmul_relu.py)
     mm = load_example(ref, "matmul")

@@ -45,6 +45,10 @@ def test_patch_tilelang_context_manager():
     (K.softmax, (16384, 512), "softmax", {"rows": 16384, "cols": 512}),
     (K.softmax, (9, 113), "softmax", {"rows": 9, "cols": 113}),
     (K.rmsnorm, (4096, 1024), "rmsnorm", {"rows": 4096, "cols": 1024, "eps": 1e-6}),
+    (K.layernorm, (4096, 1024), "layernorm", {"rows": 4096, "cols": 1024, "eps": 1e-5, "inv_n": 1.0 / 1024}),
+    (K.layernorm, (131, 100, 1e-6), "layernorm", {"rows": 131, "cols": 100, "eps": 1e-6}),
+    (K.transpose, (65, 71), "transpose", {"m": 65, "n": 71}),
+    (K.transpose, (4096, 4096), "transpose", {"m": 4096, "n": 4096}),
     (K.matmul, (4096, 4096, 4096), "gemm", {"M": 4096, "bias_mode": 0, "relu": False, "alpha": 1.0}),
     (K.matmul_bias_relu, (256, 512, 64), "gemm", {"bias_mode": 1, "relu": True}),
     (K.matmul_scaled_bias_relu, (65, 71, 37), "gemm", {"bias_mode": 2, "relu": True, "alpha": 0.5}),
@@ -144,16 +148,28 @@ def test_partial_k_loop_is_rejected():
 
 def test_unsupported_program_raises_compile_error():
     @T.prim_func
-    def transpose(A: T.Tensor((64, 64), "float32"), B: T.Tensor((64, 64), "float32")):
-        with T.Kernel(2, 2, threads=128) as (bx, by):
+    def fused_multiply_add(A: T.Tensor((1024,), "float32"), B: T.Tensor((1024,), "float32"),
+                           C: T.Tensor((1024,), "float32"), D: T.Tensor((1024,), "float32")):
+        with T.Kernel(4, threads=256) as bx:
+            for i in T.Parallel(256):
+                D[bx * 256 + i] = A[bx * 256 + i] * B[bx * 256 + i] + C[bx * 256 + i]
+
+    with pytest.raises(CompileError, match="not one of the op families"):
+        ntilang.compile(fused_multiply_add)
+
+
+def test_transpose_with_store_load_form_is_recognised():
+    @T.prim_func
+    def transpose(A: T.Tensor((64, 96), "float32"), B: T.Tensor((96, 64), "float32")):
+        with T.Kernel(2, 3, threads=128) as (bx, by):
             tile = T.alloc_shared((32, 32), "float32")
             for i, j in T.Parallel(32, 32):
                 tile[i, j] = A[bx * 32 + i, by * 32 + j]
             for i, j in T.Parallel(32, 32):
                 B[by * 32 + i, bx * 32 + j] = tile[j, i]
 
-    with pytest.raises(CompileError, match="not one of the op families"):
-        ntilang.compile(transpose)
+    kern = ntilang.compile(transpose)
+    assert kern.spec.family == "transpose" and kern.spec.params == {"m": 64, "n": 96}
 
 
 def test_softmax_without_padding_and_with_copy_load():
@@ -282,10 +298,49 @@ def test_reference_examples_are_recognised():
     expect = {
         ("vector_add", ()): "elementwise", ("cumsum", ()): "cumsum", ("softmax", ()): "softmax",
         ("rmsnorm", ()): "rmsnorm", ("matmul", ()): "gemm", ("matmul_relu", ()): "gemm",
-        ("flash_attention", ()): "fa2",
+        ("flash_attention", ()): "fa2", ("layernorm", ()): "layernorm", ("transpose", ()): "transpose",
     }
     for (name, args), family in expect.items():
         kern = getattr(load(name), name)(*args)
         assert kern.spec.family == family, name
     fa = load("flash_attention").flash_attention(8, 32, 4096, 128, is_causal=True)
     assert fa.spec.params["causal"] is True
+
+
+def test_layernorm_with_wrong_variance_is_not_recognised():
+    """sum(x*x) in place of sum((x - mean)^2) is RMS-style, not LayerNorm: reject it."""
+    width, cols, rows_per_block = 128, 100, 4
+
+    @T.prim_func
+    def not_layernorm(X: T.Tensor((8, cols), "float32"), G: T.Tensor((cols,), "float32"),
+                      Bb: T.Tensor((cols,), "float32"), Y: T.Tensor((8, cols), "float32")):
+        with T.Kernel(T.ceildiv(8, rows_per_block), threads=128) as b:
+            xs = T.alloc_fragment((rows_per_block, width), "float32")
+            sq = T.alloc_fragment((rows_per_block, width), "float32")
+            acc = T.alloc_fragment((rows_per_block,), "float32")
+            var = T.alloc_fragment((rows_per_block,), "float32")
+            for r, c in T.Parallel(rows_per_block, width):
+                xs[r, c] = X[b * rows_per_block + r, c] if c < cols else 0.0
+                sq[r, c] = xs[r, c] * xs[r, c]
+            T.reduce_sum(xs, acc, dim=1)
+            T.reduce_sum(sq, var, dim=1)
+            for r, c in T.Parallel(rows_per_block, width):
+                if c < cols:
+                    Y[b * rows_per_block + r, c] = ((xs[r, c] - acc[r] * 0.01) * T.rsqrt(var[r] * 0.01 + 1e-5)) * G[c] + Bb[c]
+
+    with pytest.raises(CompileError):
+        tilelang.compile(not_layernorm)
+
+
+def test_transpose_with_untransposed_read_is_not_recognised():
+    @T.prim_func
+    def copy_not_transpose(A: T.Tensor((64, 64), "float32"), B: T.Tensor((64, 64), "float32")):
+        with T.Kernel(2, 2, threads=128) as (bx, by):
+            t = T.alloc_shared((32, 32), "float32")
+            for i, j in T.Parallel(32, 32):
+                T.copy(A[bx * 32 + i, by * 32 + j], t[i, j])
+            for i, j in T.Parallel(32, 32):
+                B[by * 32 + i, bx * 32 + j] = t[i, j]
+
+    with pytest.raises(CompileError):
+        tilelang.compile(copy_not_transpose)

@@ -1,4 +1,4 @@
-"""GPU parity for the memory-bound families: vector add, cumsum, softmax, RMSNorm.
+"""GPU parity for the memory-bound families: vector add, cumsum, softmax, RMSNorm, LayerNorm, transpose.
 
 Every kernel runs through the reference-compatible surface (``ntilang.compile`` / ``jit``
 factories -> ``CompiledKernel.__call__`` -> the C ABI of libntl_kernels.so) and is compared
@@ -212,6 +212,78 @@ def test_rmsnorm_baseline_size(torch_cuda):
                                rtol=1e-5, atol=1e-7)
     ref = x * torch.rsqrt(x.pow(2).mean(dim=-1, keepdim=True) + 1e-6) * w
     torch.testing.assert_close(y, ref, rtol=1e-4, atol=1e-5)
+
+
+# ---------------------------------------------------------------------------- LayerNorm
+# Bar: within 1e-5 relative plus 1e-6 absolute of the oracle and of the reference evaluator's
+# golden vectors (the evaluator sums pairwise, the kernel and oracle with the emitted kernel's
+# tree; outputs near zero come from cancellation in d * rstd * w + b).
+
+
+@pytest.mark.parametrize("case", ["layernorm_6x1024", "layernorm_5x768", "layernorm_3x100"])
+def test_layernorm_golden(torch_cuda, case):
+    torch = torch_cuda
+    g = golden(case)
+    rows, cols = g["x"].shape
+    kern = K.layernorm(rows, cols, float(g["eps"]))
+    y = kern(to_gpu(torch, g["x"]), to_gpu(torch, g["w"]), to_gpu(torch, g["b"])).cpu().numpy()
+    np.testing.assert_allclose(y, g["y"], rtol=1e-5, atol=1e-6)
+
+
+@pytest.mark.parametrize("rows,cols", [(1, 1), (3, 5), (131, 256), (131, 768), (4, 2048), (3, 3000), (2, 16384)])
+def test_layernorm_shapes(torch_cuda, rows, cols):
+    torch = torch_cuda
+    rng = np.random.default_rng(rows * cols + 1)
+    x = (rng.normal(size=(rows, cols)) * 3.0 + 1.0).astype(np.float32)
+    w = rng.normal(1.0, 0.1, size=cols).astype(np.float32)
+    b = rng.normal(0.0, 0.1, size=cols).astype(np.float32)
+    y = K.layernorm(rows, cols, 1e-5)(to_gpu(torch, x), to_gpu(torch, w), to_gpu(torch, b)).cpu().numpy()
+    np.testing.assert_allclose(y, rowops.layernorm(x, w, b, 1e-5), rtol=1e-5, atol=1e-6)
+
+
+@pytest.mark.parametrize("n", [256, 512, 768])
+def test_layernorm_reference_test_shape(torch_cuda, n):
+    """The reference's GPU test shape and bar (tests/test_llm_operators.py:76-100)."""
+    torch = torch_cuda
+    import torch.nn.functional as F
+
+    x = torch.randn(131, n, device="cuda")
+    w = torch.randn(n, device="cuda")
+    b = torch.randn(n, device="cuda")
+    y = torch.empty_like(x)
+    K.layernorm(131, n, 1e-5)(x, w, b, y)
+    torch.testing.assert_close(y, F.layer_norm(x, (n,), weight=w, bias=b, eps=1e-5), rtol=1e-4, atol=1e-5)
+
+
+def test_layernorm_baseline_size(torch_cuda):
+    torch = torch_cuda
+    g = torch.Generator(device="cuda").manual_seed(0)
+    x = torch.randn(4096, 1024, device="cuda", generator=g)
+    w = torch.randn(1024, device="cuda", generator=g) * 0.1 + 1.0
+    b = torch.randn(1024, device="cuda", generator=g) * 0.1
+    y = K.layernorm(4096, 1024, 1e-5)(x, w, b)
+    np.testing.assert_allclose(y.cpu().numpy(), rowops.layernorm(x.cpu().numpy(), w.cpu().numpy(), b.cpu().numpy(),
+                                                                1e-5), rtol=1e-5, atol=1e-6)
+
+
+# ---------------------------------------------------------------------------- transpose (bit-exact)
+
+
+@pytest.mark.parametrize("case", ["transpose_65x71", "transpose_33x130"])
+def test_transpose_golden(torch_cuda, case):
+    torch = torch_cuda
+    g = golden(case)
+    m, n = g["a"].shape
+    out = K.transpose(m, n)(to_gpu(torch, g["a"])).cpu().numpy()
+    assert np.array_equal(out, g["b"])
+
+
+@pytest.mark.parametrize("m,n", [(1, 1), (1, 100), (100, 1), (65, 71), (1000, 33), (4096, 4096)])
+def test_transpose_shapes(torch_cuda, m, n):
+    torch = torch_cuda
+    a = torch.randn(m, n, device="cuda")
+    b = K.transpose(m, n)(a)
+    torch.testing.assert_close(b, a.T, rtol=0, atol=0)
 
 
 def test_native_launches_counted(torch_cuda):

@@ -68,6 +68,26 @@ def test_rmsnorm_within_1e5(case):
         np.testing.assert_allclose(got, g["y"], rtol=1e-5, atol=1e-7)
 
 
+@pytest.mark.parametrize("case", ["layernorm_6x1024", "layernorm_5x768", "layernorm_3x100"])
+def test_layernorm_within_tolerance(case):
+    """The reference evaluator sums with NumPy's pairwise add.reduce; the oracle (and the GPU
+    kernel) follow the emitted kernel's perfect tree, so they agree to rounding: 1e-5 relative
+    plus 1e-6 absolute (outputs near zero come from cancellation in d * rstd * w + b)."""
+    g = golden(case)
+    eps = float(g["eps"])
+    oracle_np = O.layernorm_rows(g["x"], g["w"], g["b"], eps)
+    oracle_c = rowops.layernorm(g["x"], g["w"], g["b"], eps)
+    np.testing.assert_array_equal(oracle_np.view(np.uint32), oracle_c.view(np.uint32))
+    np.testing.assert_allclose(oracle_np, g["y"], rtol=1e-5, atol=1e-6)
+
+
+@pytest.mark.parametrize("case", ["transpose_65x71", "transpose_33x130"])
+def test_transpose_bit_exact(case):
+    g = golden(case)
+    np.testing.assert_array_equal(O.transpose(g["a"]), g["b"])
+    np.testing.assert_array_equal(rowops.transpose(g["a"]), g["b"])
+
+
 def test_gemm_against_reference_evaluator():
     g = golden("gemm_65x71x37")
     np.testing.assert_allclose(O.gemm(g["a"], g["b"]), g["c"], rtol=1e-5, atol=1e-4)
