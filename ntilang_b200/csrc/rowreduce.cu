@@ -284,48 +284,90 @@ __device__ __forceinline__ void centre(float (&v)[NCH][4], float mean, int64_t c
     }
 }
 
+// w and b are read by every row of the block: the block stages both in shared memory once
+// (2 * cols floats) after the dependent-launch wait, so the epilogue reads them at shared-
+// memory latency and the compiler does not hold 8 * NCH weight registers across the row.
+// Up to 8 chunks the kernel is held to 64 registers, two 512-thread blocks per SM.
 template <int NCH, bool VEC>
-__global__ void __launch_bounds__(kLayernormWarpsPerBlock * 32) layernorm_rows_warp(const float* __restrict__ x,
-                                                                                    const float* __restrict__ w,
-                                                                                    const float* __restrict__ b,
-                                                                                    float* __restrict__ y,
-                                                                                    int64_t rows, int64_t cols,
-                                                                                    float eps, float inv_n) {
+__global__ void __launch_bounds__(kLayernormWarpsPerBlock * 32, (NCH <= 8 ? 2 : 1))
+    layernorm_rows_warp(const float* __restrict__ x, const float* __restrict__ w, const float* __restrict__ b,
+                        float* __restrict__ y, int64_t rows, int64_t cols, float eps, float inv_n) {
+  extern __shared__ float4 wb_s4[];  // w[cols] then b[cols]
+  float* wb_s = reinterpret_cast<float*>(wb_s4);
   const int lane = threadIdx.x & 31;
   const int64_t row = static_cast<int64_t>(blockIdx.x) * kLayernormWarpsPerBlock + (threadIdx.x >> 5);
-  if (lane == 0 && row < rows) prefetch_l2(x + row * cols, cols * 4);
+  const bool live = row < rows;
+  if (lane == 0 && live) prefetch_l2(x + row * cols, cols * 4);
   if (threadIdx.x == 32) prefetch_l2(w, cols * 4);
   if (threadIdx.x == 64) prefetch_l2(b, cols * 4);
   pdl_wait();
   pdl_trigger();
-  if (row >= rows) return;
+  const int n = static_cast<int>(cols);  // <= 2048 on this path
+  if (VEC) {
+    const int nq = n >> 2;
+    for (int i = threadIdx.x; i < nq; i += kLayernormWarpsPerBlock * 32) {
+      wb_s4[i] = __ldg(reinterpret_cast<const float4*>(w) + i);
+      wb_s4[nq + i] = __ldg(reinterpret_cast<const float4*>(b) + i);
+    }
+  } else {
+    for (int i = threadIdx.x; i < n; i += kLayernormWarpsPerBlock * 32) {
+      wb_s[i] = __ldg(w + i);
+      wb_s[n + i] = __ldg(b + i);
+    }
+  }
   const float* xr = x + row * cols;
-  float* yr = y + row * cols;
   float v[NCH][4];
+  if (live) {
 #pragma unroll
-  for (int c = 0; c < NCH; ++c) load4<VEC>(xr, static_cast<int64_t>(c) * 128 + lane * 4, cols, 0.0f, v[c]);
+    for (int c = 0; c < NCH; ++c) {
+      const int col = c * 128 + lane * 4;
+      if (VEC) {  // n % 4 == 0: a 4-column group is wholly inside or outside the row
+        float4 t = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        if (col < n) t = __ldcs(reinterpret_cast<const float4*>(xr + col));
+        v[c][0] = t.x, v[c][1] = t.y, v[c][2] = t.z, v[c][3] = t.w;
+      } else {
+        load4<false>(xr, col, cols, 0.0f, v[c]);
+      }
+    }
+  }
+  __syncthreads();
+  if (!live) return;
   float s[NCH];
 #pragma unroll
   for (int c = 0; c < NCH; ++c) s[c] = warp_tree_sum(lane_pair_sum(v[c]));
   const float mean = __fmul_rn(chunk_tree<NCH>(s), inv_n);
-  centre<NCH>(v, mean, lane * 4, 128, cols);
 #pragma unroll
   for (int c = 0; c < NCH; ++c) {
     float q[4];
 #pragma unroll
-    for (int e = 0; e < 4; ++e) q[e] = __fmul_rn(v[c][e], v[c][e]);
+    for (int e = 0; e < 4; ++e) {
+      v[c][e] = (c * 128 + lane * 4 + e < n) ? __fsub_rn(v[c][e], mean) : 0.0f;
+      q[e] = __fmul_rn(v[c][e], v[c][e]);
+    }
     s[c] = warp_tree_sum(lane_pair_sum(q));
   }
   const float rstd = rsqrtf(__fadd_rn(__fmul_rn(chunk_tree<NCH>(s), inv_n), eps));
+  float* yr = y + row * cols;
 #pragma unroll
   for (int c = 0; c < NCH; ++c) {
-    const int64_t col = static_cast<int64_t>(c) * 128 + lane * 4;
+    const int col = c * 128 + lane * 4;
+    if (col >= n) continue;
     float wv[4], bv[4];
-    load_w4<VEC>(w, col, cols, wv);
-    load_w4<VEC>(b, col, cols, bv);
+    if (VEC) {
+      const float4 tw = wb_s4[col >> 2], tb = wb_s4[(n + col) >> 2];
+      wv[0] = tw.x, wv[1] = tw.y, wv[2] = tw.z, wv[3] = tw.w;
+      bv[0] = tb.x, bv[1] = tb.y, bv[2] = tb.z, bv[3] = tb.w;
+    } else {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        wv[e] = col + e < n ? wb_s[col + e] : 0.0f;
+        bv[e] = col + e < n ? wb_s[n + col + e] : 0.0f;
+      }
+    }
 #pragma unroll
     for (int e = 0; e < 4; ++e) v[c][e] = __fadd_rn(__fmul_rn(__fmul_rn(v[c][e], rstd), wv[e]), bv[e]);
-    store4<VEC>(yr, col, cols, v[c]);
+    if (VEC) __stcs(reinterpret_cast<float4*>(yr + col), make_float4(v[c][0], v[c][1], v[c][2], v[c][3]));
+    else store4<false>(yr, col, cols, v[c]);
   }
 }
 
@@ -400,18 +442,18 @@ constexpr int64_t kMaxCtaCols = 16384;   // 16 chunks of 1024 per CTA
 template <class WarpK, class CtaK>
 struct Dispatch;
 
-#define NTL_ROW_DISPATCH(KW, KC, VEC, WPB, ...)                                                         \
+#define NTL_ROW_DISPATCH(KW, KC, VEC, WPB, WSMEM, ...)                                                         \
   do {                                                                                                  \
     const int64_t nch = (cols + 127) / 128;                                                             \
     if (cols <= kMaxWarpCols) {                                                                         \
       const int64_t blocks = (rows + (WPB)-1) / (WPB);                                                  \
       NTL_REQUIRE(blocks <= 0x7fffffff, NTL_ERR_UNSUPPORTED, "too many rows");                         \
       dim3 ntl_grid_(static_cast<unsigned>(blocks)), ntl_block_((WPB)*32);                                               \
-      if (nch <= 1) ntl_launch_pdl(KW<1, VEC>, ntl_grid_, ntl_block_, 0, s, __VA_ARGS__);                                \
-      else if (nch <= 2) ntl_launch_pdl(KW<2, VEC>, ntl_grid_, ntl_block_, 0, s, __VA_ARGS__);                           \
-      else if (nch <= 4) ntl_launch_pdl(KW<4, VEC>, ntl_grid_, ntl_block_, 0, s, __VA_ARGS__);                           \
-      else if (nch <= 8) ntl_launch_pdl(KW<8, VEC>, ntl_grid_, ntl_block_, 0, s, __VA_ARGS__);                           \
-      else ntl_launch_pdl(KW<16, VEC>, ntl_grid_, ntl_block_, 0, s, __VA_ARGS__);                                        \
+      if (nch <= 1) ntl_launch_pdl(KW<1, VEC>, ntl_grid_, ntl_block_, (WSMEM), s, __VA_ARGS__);                                \
+      else if (nch <= 2) ntl_launch_pdl(KW<2, VEC>, ntl_grid_, ntl_block_, (WSMEM), s, __VA_ARGS__);                           \
+      else if (nch <= 4) ntl_launch_pdl(KW<4, VEC>, ntl_grid_, ntl_block_, (WSMEM), s, __VA_ARGS__);                           \
+      else if (nch <= 8) ntl_launch_pdl(KW<8, VEC>, ntl_grid_, ntl_block_, (WSMEM), s, __VA_ARGS__);                           \
+      else ntl_launch_pdl(KW<16, VEC>, ntl_grid_, ntl_block_, (WSMEM), s, __VA_ARGS__);                                        \
     } else {                                                                                            \
       NTL_REQUIRE(rows <= 0x7fffffff, NTL_ERR_UNSUPPORTED, "too many rows");                           \
       const int64_t cch = (cols + 1023) / 1024;                                                         \
@@ -434,9 +476,9 @@ extern "C" int ntl_softmax_f32(const float* x, float* y, int64_t rows, int64_t c
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const bool vec = (cols % 4 == 0) && ntl_aligned(x, 16) && ntl_aligned(y, 16);
   if (vec)
-    NTL_ROW_DISPATCH(softmax_rows_warp, softmax_rows_cta, true, kSoftmaxWarpsPerBlock, x, y, rows, cols);
+    NTL_ROW_DISPATCH(softmax_rows_warp, softmax_rows_cta, true, kSoftmaxWarpsPerBlock, 0, x, y, rows, cols);
   else
-    NTL_ROW_DISPATCH(softmax_rows_warp, softmax_rows_cta, false, kSoftmaxWarpsPerBlock, x, y, rows, cols);
+    NTL_ROW_DISPATCH(softmax_rows_warp, softmax_rows_cta, false, kSoftmaxWarpsPerBlock, 0, x, y, rows, cols);
   ntl_note_launch();
   return ntl_check_launch("softmax launch");
 }
@@ -451,9 +493,9 @@ extern "C" int ntl_rmsnorm_f32(const float* x, const float* w, float* y, int64_t
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const bool vec = (cols % 4 == 0) && ntl_aligned(x, 16) && ntl_aligned(y, 16) && ntl_aligned(w, 16);
   if (vec)
-    NTL_ROW_DISPATCH(rmsnorm_rows_warp, rmsnorm_rows_cta, true, kRmsnormWarpsPerBlock, x, w, y, rows, cols, eps, inv_n);
+    NTL_ROW_DISPATCH(rmsnorm_rows_warp, rmsnorm_rows_cta, true, kRmsnormWarpsPerBlock, 0, x, w, y, rows, cols, eps, inv_n);
   else
-    NTL_ROW_DISPATCH(rmsnorm_rows_warp, rmsnorm_rows_cta, false, kRmsnormWarpsPerBlock, x, w, y, rows, cols, eps, inv_n);
+    NTL_ROW_DISPATCH(rmsnorm_rows_warp, rmsnorm_rows_cta, false, kRmsnormWarpsPerBlock, 0, x, w, y, rows, cols, eps, inv_n);
   ntl_note_launch();
   return ntl_check_launch("rmsnorm launch");
 }
@@ -468,12 +510,13 @@ extern "C" int ntl_layernorm_f32(const float* x, const float* w, const float* b,
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const bool vec = (cols % 4 == 0) && ntl_aligned(x, 16) && ntl_aligned(y, 16) && ntl_aligned(w, 16) &&
                    ntl_aligned(b, 16);
+  const size_t wb_bytes = 2 * static_cast<size_t>(cols) * sizeof(float);  // warp path only: cols <= 2048
   if (vec)
-    NTL_ROW_DISPATCH(layernorm_rows_warp, layernorm_rows_cta, true, kLayernormWarpsPerBlock, x, w, b, y, rows, cols,
-                     eps, inv_n);
+    NTL_ROW_DISPATCH(layernorm_rows_warp, layernorm_rows_cta, true, kLayernormWarpsPerBlock, wb_bytes, x, w, b, y,
+                     rows, cols, eps, inv_n);
   else
-    NTL_ROW_DISPATCH(layernorm_rows_warp, layernorm_rows_cta, false, kLayernormWarpsPerBlock, x, w, b, y, rows,
-                     cols, eps, inv_n);
+    NTL_ROW_DISPATCH(layernorm_rows_warp, layernorm_rows_cta, false, kLayernormWarpsPerBlock, wb_bytes, x, w, b, y,
+                     rows, cols, eps, inv_n);
   ntl_note_launch();
   return ntl_check_launch("layernorm launch");
 }

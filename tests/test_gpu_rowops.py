@@ -230,7 +230,8 @@ def test_layernorm_golden(torch_cuda, case):
     np.testing.assert_allclose(y, g["y"], rtol=1e-5, atol=1e-6)
 
 
-@pytest.mark.parametrize("rows,cols", [(1, 1), (3, 5), (131, 256), (131, 768), (4, 2048), (3, 3000), (2, 16384)])
+@pytest.mark.parametrize("rows,cols", [(1, 1), (3, 5), (131, 256), (131, 768), (4, 2048), (37, 1030), (40, 999),
+                                       (3, 3000), (2, 16384)])
 def test_layernorm_shapes(torch_cuda, rows, cols):
     torch = torch_cuda
     rng = np.random.default_rng(rows * cols + 1)
@@ -278,12 +279,32 @@ def test_transpose_golden(torch_cuda, case):
     assert np.array_equal(out, g["b"])
 
 
-@pytest.mark.parametrize("m,n", [(1, 1), (1, 100), (100, 1), (65, 71), (1000, 33), (4096, 4096)])
+# (n % 4, m % 4) select the vector or scalar side of the kernel: all four pairings, partial
+# 64x64 tiles on either edge, and a full-size square.
+@pytest.mark.parametrize("m,n", [(1, 1), (1, 100), (100, 1), (65, 71), (64, 71), (65, 72), (1000, 33), (130, 260),
+                                 (4096, 4096)])
 def test_transpose_shapes(torch_cuda, m, n):
     torch = torch_cuda
     a = torch.randn(m, n, device="cuda")
     b = K.transpose(m, n)(a)
     torch.testing.assert_close(b, a.T, rtol=0, atol=0)
+
+
+@pytest.mark.parametrize("a_off,b_off", [(1, 0), (0, 1), (1, 1)])
+def test_transpose_unaligned_pointers(torch_cuda, a_off, b_off):
+    """Buffers that start 4 bytes past a 16-byte boundary take the element-wise side."""
+    torch = torch_cuda
+    from ntilang_b200 import _lib
+
+    m, n = 72, 136
+    abuf = torch.randn(m * n + 1, device="cuda")
+    bbuf = torch.full((m * n + 1,), -1.0, device="cuda")
+    _lib.call("ntl_transpose_f32", abuf.data_ptr() + 4 * a_off, bbuf.data_ptr() + 4 * b_off, m, n,
+              torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    a = abuf[a_off:a_off + m * n].view(m, n)
+    assert torch.equal(bbuf[b_off:b_off + m * n].view(n, m), a.T)
+    assert bbuf[0 if b_off else m * n].item() == -1.0  # nothing written outside B
 
 
 def test_native_launches_counted(torch_cuda):
