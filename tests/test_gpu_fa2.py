@@ -68,6 +68,20 @@ def test_fa2_ragged_sequence(torch_cuda, seq, causal):
     torch.testing.assert_close(out.float(), sdpa_fp32(torch, q, k, v, causal), rtol=0, atol=ATOL)
 
 
+# More (batch, head, 256-query block) units than SMs: every persistent CTA runs several units
+# back to back, including units whose second 128-row query tile lies past the sequence end
+# (seq 600: the last block has one live tile).
+@pytest.mark.parametrize("seq", [600, 700])
+@pytest.mark.parametrize("causal", [False, True])
+@pytest.mark.parametrize("dim", [64, 128])
+def test_fa2_several_units_per_cta(torch_cuda, seq, causal, dim):
+    torch = torch_cuda
+    gen = torch.Generator(device="cuda").manual_seed(seq + dim)
+    q, k, v = (torch.randn(3, 67, seq, dim, device="cuda", generator=gen, dtype=torch.float16) for _ in range(3))
+    out = K.flash_attention(3, 67, seq, dim, causal)(q, k, v)
+    torch.testing.assert_close(out.float(), sdpa_fp32(torch, q, k, v, causal), rtol=0, atol=ATOL)
+
+
 def test_fa2_matches_reference_blockwise_algorithm(torch_cuda):
     torch = torch_cuda
     rng = np.random.default_rng(3)
