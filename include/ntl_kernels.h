@@ -136,6 +136,17 @@ int ntl_gemm_f16_f32_noalloc(const uint16_t* a, const uint16_t* b, float* c, con
 int ntl_fa2_fwd_f16(const uint16_t* q, const uint16_t* k, const uint16_t* v, uint16_t* o, int64_t batch,
                     int64_t heads, int64_t seq, int64_t dim, float scale_log2, int causal, ntl_stream_t stream);
 
+/* Generic elementwise programs (outside the families above): run-time compiled kernels.
+ * ntl_rtc_build compiles CUDA C `source` (one extern "C" __global__ function named
+ * `kernel_name`) with NVRTC for sm_100a on the host, no GPU needed, and returns a handle;
+ * ntl_rtc_launch runs it as a 1-D grid of grid_x blocks of block_x threads on `stream`, with
+ * `args` the kernel's argument pointers in cuLaunchKernel form.  Together they replace the
+ * reference's CompiledKernel.build() / executable(*ffi_arguments) pair for such programs
+ * (python/ntilang/compiler.py:51-71, :197).  A compile error returns NTL_ERR_INVALID with the
+ * NVRTC log in ntl_last_error(). */
+int ntl_rtc_build(const char* source, const char* kernel_name, uint64_t* handle_out);
+int ntl_rtc_launch(uint64_t handle, uint64_t grid_x, uint32_t block_x, void** args, ntl_stream_t stream);
+
 /* Device status word of the bounded waits in the tcgen05 kernels on the current device:
  * 0 = no timeout since the last clear, else a code naming the wait that gave up.  Reading
  * it synchronises the device.  No reference counterpart (its kernels have no bounded

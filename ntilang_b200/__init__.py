@@ -11,12 +11,14 @@ from .compat import patch_tilelang
 from .compiler import CompiledKernel, DynamicJitKernel, compile
 from .ir import CompileError, SymDim
 from .language import jit
+from .pipeline import Compiler
 
 __version__ = "0.1.0"
 __all__ = [
     "AutoTuner",
     "CompileError",
     "CompiledKernel",
+    "Compiler",
     "DynamicJitKernel",
     "SymDim",
     "autotune",

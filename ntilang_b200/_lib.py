@@ -43,6 +43,9 @@ SIGNATURES = {
                                                 ctypes.c_void_p]),
     "ntl_fa2_fwd_f16": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, c_i64,
                                        c_i64, c_i64, c_i64, ctypes.c_float, ctypes.c_int, ctypes.c_void_p]),
+    "ntl_rtc_build": (ctypes.c_int, [ctypes.c_char_p, ctypes.c_char_p, ctypes.POINTER(ctypes.c_uint64)]),
+    "ntl_rtc_launch": (ctypes.c_int, [ctypes.c_uint64, ctypes.c_uint64, ctypes.c_uint32,
+                                      ctypes.POINTER(ctypes.c_void_p), ctypes.c_void_p]),
     "ntl_device_status": (ctypes.c_int, [ctypes.POINTER(ctypes.c_uint32)]),
     "ntl_clear_device_status": (ctypes.c_int, []),
     "ntl_set_wait_limit": (ctypes.c_int, [c_i64]),

@@ -70,7 +70,7 @@ def build_library(force: bool = False, verbose: bool = False) -> Path:
     if failures:
         raise RuntimeError("nvcc failed:\n" + "\n".join(failures))
     tmp = LIB.with_suffix(".so.tmp")
-    cmd = [nvcc, *ARCH, "-shared", "--cudart", "static", "-o", str(tmp), *map(str, objects)]
+    cmd = [nvcc, *ARCH, "-shared", "--cudart", "static", "-o", str(tmp), *map(str, objects), "-ldl"]
     res = subprocess.run(cmd, capture_output=True, text=True)
     if res.returncode != 0:
         raise RuntimeError("link failed:\n" + res.stdout + res.stderr)

@@ -3,8 +3,10 @@
 Same contract as the reference's ``python/ntilang/compiler.py``:
 
 * ``compile(prim_func, target=, out_idx=)`` (:340-355) reads the program and normalises
-  ``out_idx``; here it also recognises the op family (``recognize.recognize``) instead
-  of generating CuTe source.
+  ``out_idx``; instead of generating CuTe source it recognises the op family
+  (``recognize.recognize``, a prebuilt sm_100a kernel) or, for any other elementwise
+  program, generates CUDA C compiled by NVRTC (``pointwise.lower``).  ``source`` /
+  ``save()`` give a standalone launcher module (``export.standalone_module``).
 * ``CompiledKernel.__call__`` (:134-200) allocates ``out_idx`` outputs with
   ``torch.empty`` on the first CUDA input's device (:109-132), checks every tensor
   (CUDA device, shape, dtype, row-major contiguity, 16-byte alignment, disjoint
@@ -29,7 +31,10 @@ from .compat import normalize_out_idx, resolve_target, torch_dtype_for
 from .frontend import Program, read_program
 from .ir import DTYPES, CompileError, ScalarParameter, SymDim
 from .language import PrimFunc, SymbolicDim, SymbolicTensorSpec
+from .export import standalone_module
 from .launch import describe, launch
+from .pointwise import lower as lower_pointwise
+from .pointwise import validate_scalar
 from .recognize import OpSpec, recognize
 
 
@@ -42,30 +47,40 @@ def _torch():
 class CompiledKernel:
     ir: Program
     target: str
-    source: str
+    source: str  # the standalone launcher module save() writes (ntilang_b200.export)
     out_idx: tuple = ()
     spec: OpSpec = None
     _built: bool = field(default=False, init=False, repr=False)
+
+    has_gpu_module = True
 
     @property
     def cache_key(self) -> str:
         return hashlib.sha256(self.source.encode("utf-8")).hexdigest()
 
     def get_kernel_source(self) -> str:
-        return self.source
+        """Device code: the generated CUDA C for a generic elementwise program, else the launch
+        plan of the prebuilt sm_100a kernel in libntl_kernels.so."""
+        if self.spec is not None and self.spec.family == "pointwise":
+            return self.spec.params["kernel"].source
+        return describe(self.spec, self.ir.name, self.target)
 
     def get_host_source(self) -> str:
         return self.source
 
     def save(self, path) -> Path:
+        """Write the standalone launcher module (python/ntilang/compiler.py:44-49)."""
         path = Path(path)
         path.parent.mkdir(parents=True, exist_ok=True)
         path.write_text(self.source, encoding="utf-8", newline="\n")
         return path
 
     def build(self):
-        """Load libntl_kernels.so (the kernels are compiled ahead of time for sm_100a)."""
+        """Load libntl_kernels.so (the recognised kernels are compiled ahead of time for
+        sm_100a); a generic elementwise program is also compiled by NVRTC here."""
         handle = _lib.lib()
+        if self.spec is not None and self.spec.family == "pointwise":
+            self.spec.params["kernel"].build()
         self._built = True
         return handle
 
@@ -138,7 +153,12 @@ class CompiledKernel:
                 raise ValueError(f"Unbound symbolic dimensions: {', '.join(missing)}")
         devices = set()
         ranges = []
+        checked = []
         for tensor, param in zip(arguments, params):
+            if isinstance(param, ScalarParameter):
+                checked.append(validate_scalar(tensor, param))
+                continue
+            checked.append(tensor)
             if not hasattr(tensor, "__dlpack_device__") or tensor.__dlpack_device__()[0] != 2:
                 raise TypeError(f"{param.name} must be a CUDA tensor supporting DLPack")
             devices.add(tensor.__dlpack_device__()[1])
@@ -161,13 +181,15 @@ class CompiledKernel:
             ranges.append((pointer, pointer + size, param.name))
         if len(devices) > 1:
             raise ValueError("All tensor arguments must be on the same CUDA device")
+        if not devices:
+            raise TypeError("a kernel launch needs at least one CUDA tensor argument")
         if not self._built:
             self.build()
         torch = _torch()
-        device = arguments[0].device
+        device = next(a.device for a, p in zip(arguments, params) if not isinstance(p, ScalarParameter))
         with torch.cuda.device(device):
             stream = torch.cuda.current_stream(device).cuda_stream
-            launch(self.spec, arguments, stream)
+            launch(self.spec, checked, stream, bindings)
         if allocated is not None:
             return allocated[0] if len(allocated) == 1 else tuple(allocated)
         return None
@@ -185,15 +207,33 @@ class CompiledKernel:
         return bindings
 
 
+def lower_program(prog: Program) -> OpSpec:
+    """The op a program runs: a recognised family (prebuilt sm_100a kernel), else a generic
+    elementwise kernel generated as CUDA C for NVRTC; ``CompileError`` when neither applies."""
+    try:
+        return recognize(prog)
+    except CompileError as family_error:
+        try:
+            kernel = lower_pointwise(prog)
+        except CompileError as pointwise_error:
+            raise CompileError(f"{family_error}\n  pointwise: {pointwise_error}") from None
+        return OpSpec("pointwise", {"kernel": kernel, "points": kernel.points}, {})
+
+
+def make_kernel(prog: Program, spec: OpSpec, target: str, out_idx) -> CompiledKernel:
+    normalized = normalize_out_idx(out_idx, prog.params)
+    source = standalone_module(spec, prog, prog.name, target, str(_lib.library_path()))
+    return CompiledKernel(prog, target, source, out_idx=normalized, spec=spec)
+
+
 def compile(program: PrimFunc, *, target="sm_100a", out_idx=None, pass_configs=None) -> CompiledKernel:
-    """Read and recognise a ``@T.prim_func``; the sm_100a kernels are prebuilt, so nothing
-    is compiled per program.  Unrecognised programs raise ``CompileError``."""
+    """Read a ``@T.prim_func`` and pick its kernel: a recognised op family (prebuilt for
+    sm_100a, nothing compiled per program) or a generic elementwise kernel (CUDA C, compiled
+    by NVRTC on first launch).  Other programs raise ``CompileError``."""
     del pass_configs
     resolved = resolve_target(target)
     prog = read_program(program)
-    spec = recognize(prog)
-    normalized = normalize_out_idx(out_idx, prog.params)
-    return CompiledKernel(prog, resolved, describe(spec, prog.name, resolved), out_idx=normalized, spec=spec)
+    return make_kernel(prog, lower_program(prog), resolved, out_idx)
 
 
 class DynamicJitKernel:

@@ -156,7 +156,17 @@ class Store:
 
 
 @dataclass
+class Atomic:
+    op: str  # add | max | min
+    buf: str
+    idx: tuple
+    value: object
+
+
+@dataclass
 class Let:
+    """Assignment to a mutable kernel scalar (``T.alloc_var``), or a loop-carried update."""
+
     name: str
     value: object
 
@@ -199,9 +209,14 @@ class NotStatic(Exception):
 
 _MATH_FUNCS = {
     "exp": "exp", "exp2": "exp2", "__exp": "exp", "log": "log", "log2": "log2", "sqrt": "sqrt",
-    "rsqrt": "rsqrt", "abs": "abs", "maximum": "max", "max": "max", "minimum": "min", "min": "min",
-    "tanh": "tanh", "sigmoid": "sigmoid", "fast_rcp": "rcp", "erf": "erf",
+    "rsqrt": "rsqrt", "abs": "abs", "maximum": "maximum", "max": "max", "minimum": "minimum", "min": "min",
+    "tanh": "tanh", "sigmoid": "sigmoid", "fast_rcp": "rcp", "erf": "erf", "exp10": "exp10",
+    "log10": "log10", "log1p": "log1p", "sin": "sin", "cos": "cos", "tan": "tan", "floor": "floor",
+    "ceil": "ceil", "trunc": "trunc", "round": "round", "nearbyint": "nearbyint", "isnan": "isnan",
+    "isinf": "isinf", "isfinite": "isfinite", "pow": "pow", "fmod": "fmod", "clamp": "clamp",
+    "floordiv": "//", "floormod": "%", "truncdiv": "truncdiv", "truncmod": "truncmod",
 }
+_ATOMICS = {"atomic_add": "add", "atomic_max": "max", "atomic_min": "min"}
 
 _COPY_LIKE = {"copy"}
 _REDUCE_KINDS = {
@@ -241,7 +256,11 @@ class _Reader:
         # T.dynamic specialisation: symbolic name -> concrete value
         self.special = dict(program.specializations)
         self.kernel_names: set = set()  # names bound at kernel time (shadow env)
-        self.lets: dict = {}  # kernel-scope name -> Expr
+        self.lets: dict = {}  # kernel-scope name -> Expr (immutable binding, substituted at each use)
+        self.let_paths: dict = {}  # name -> control-flow path of its binding
+        self.path: list = []  # ids of the enclosing if-branches / loop bodies
+        self._next_block = 0
+        self.mutables: dict = {}  # T.alloc_var name -> dtype
         self.buffers: dict = {}
         self.sym_dims: dict = {}
 
@@ -366,11 +385,23 @@ class _Reader:
             self.sym_dims[value.name] = SymDim(value.name)
             return Var(f"$sym:{value.name}")
         if isinstance(node, ast.Name):
+            if node.id in self.mutables:
+                return Var(node.id)
             if node.id in self.lets:
+                bound = self.let_paths.get(node.id, ())
+                if tuple(self.path[:len(bound)]) != bound:
+                    self.fail(node, f"{node.id!r} is used outside its defining region (it is assigned inside a "
+                                    "branch or loop body); declare it with T.alloc_var")
                 return self.lets[node.id]
             if node.id in self.kernel_names:
                 return Var(node.id)
             self.fail(node, f"Unknown name {node.id!r} in kernel expression")
+        if isinstance(node, ast.BoolOp):
+            fn = "and" if isinstance(node.op, ast.And) else "or"
+            out = self.expr(node.values[0])
+            for v in node.values[1:]:
+                out = Call(fn, (out, self.expr(v)))
+            return out
         if isinstance(node, ast.BinOp):
             op = _BINSYM.get(type(node.op))
             if op is None:
@@ -384,6 +415,8 @@ class _Reader:
                 return Call("neg", (inner,))
             if isinstance(node.op, ast.UAdd):
                 return self.expr(node.operand)
+            if isinstance(node.op, ast.Not):
+                return Call("not", (self.expr(node.operand),))
             self.fail(node, "Unsupported unary operator")
         if isinstance(node, ast.Compare) and len(node.ops) == 1:
             return Cmp(_CMPSYM[type(node.ops[0])], self.expr(node.left), self.expr(node.comparators[0]))
@@ -400,15 +433,30 @@ class _Reader:
             return Load(buf, tuple(idx))
         if isinstance(node, ast.Call):
             name = self.call_name(node)
+            if name == "cast":
+                kw = {k.arg: k.value for k in node.keywords}
+                target = node.args[1] if len(node.args) > 1 else kw.get("dtype")
+                if target is None or not node.args:
+                    self.fail(node, "T.cast needs a value and a dtype")
+                return Call("cast", (self.expr(node.args[0]), Const(canonical_dtype(str(self.static(target))))))
             args = [self.expr(a) for a in node.args]
             if name in ("if_then_else", "Select"):
                 return Select(*args)
             if name in ("ceildiv", "cdiv") and len(args) == 2:
                 return Bin("//", Bin("+", args[0], Bin("-", args[1], Const(1))), args[1])
+            if name == "clamp":  # min(max(value, low), high), as the reference reads it (frontend.py:1098-1102)
+                if len(args) != 3:
+                    self.fail(node, "T.clamp takes (value, min_val, max_val)")
+                return Call("min", (Call("max", (args[0], args[1])), args[2]))
             if name in _MATH_FUNCS:
-                return Call(_MATH_FUNCS[name], tuple(args))
-            if name in ("cast",) or (name in (*_DTYPE_CALLS,)):
-                return Call("cast", tuple(args[:1]))
+                fn = _MATH_FUNCS[name]
+                if fn in ("//", "%"):
+                    return Bin(fn, *args)
+                return Call(fn, tuple(args))
+            if name in _DTYPE_CALLS:
+                return Call("cast", (args[0], Const(_DTYPE_CALLS[name])))
+            if name == "likely":
+                return args[0]
             self.fail(node, f"Unsupported call {name!r} in kernel expression")
         self.fail(node, f"Unsupported expression {type(node).__name__}")
 
@@ -469,7 +517,7 @@ class _Reader:
         params = []
         for arg in self.fdef.args.args:
             ann = self.program.function.__annotations__.get(arg.arg)
-            if isinstance(ann, str):
+            if isinstance(ann, str) and not isinstance(ann, DType):
                 try:
                     ann = eval(ann, dict(self.env))  # noqa: S307 - annotation strings of the user's own kernel
                 except Exception as exc:
@@ -565,6 +613,15 @@ class _Reader:
             out.extend(self.stmt(s))
         return out
 
+    def nested(self, stmts):
+        """A branch or loop body: bindings made inside it are not visible after it."""
+        self._next_block += 1
+        self.path.append(self._next_block)
+        try:
+            return self.block(stmts)
+        finally:
+            self.path.pop()
+
     def stmt(self, node):
         if isinstance(node, ast.Expr):
             if isinstance(node.value, ast.Constant):
@@ -581,13 +638,17 @@ class _Reader:
                 if name in ("alloc_shared", "alloc_fragment", "alloc_local"):
                     return [self.alloc(target.id, node.value, name)]
                 if name == "alloc_var":
-                    return [self.alloc_var(target.id, node.value)]
+                    return self.alloc_var(target.id, node.value)
+                if target.id in self.mutables:
+                    return [Let(target.id, simplify(self.expr(node.value)))]
                 ok, value = self.try_static(node.value)
                 if ok and not isinstance(value, (SymbolicDim,)):
                     self.env[target.id] = value
                     return []
-                # Kernel-time scalar binding: substituted at each use (single assignment).
+                # Kernel-time scalar binding: substituted at each use, valid inside the block
+                # (and the blocks nested in it) where it was made.
                 self.lets[target.id] = simplify(self.expr(node.value))
+                self.let_paths[target.id] = tuple(self.path)
                 return []
             if isinstance(target, ast.Subscript):
                 buf = self.buffer_name(target.value)
@@ -601,7 +662,7 @@ class _Reader:
                 buf = self.buffer_name(target.value)
                 idx = tuple(self.index_list(target.slice))
                 return [Store(buf, idx, simplify(Bin(op, Load(buf, idx), self.expr(node.value))))]
-            if isinstance(target, ast.Name) and target.id in self.kernel_names:
+            if isinstance(target, ast.Name) and (target.id in self.kernel_names or target.id in self.mutables):
                 value = Bin(op, Var(target.id), self.expr(node.value))
                 return [Let(target.id, simplify(value))]
             self.fail(node, "Unsupported augmented assignment")
@@ -611,7 +672,8 @@ class _Reader:
             ok, test = self.try_static(node.test)
             if ok:
                 return self.block(node.body if test else node.orelse)
-            return [If(simplify(self.expr(node.test)), self.block(node.body), self.block(node.orelse))]
+            cond = simplify(self.expr(node.test))
+            return [If(cond, self.nested(node.body), self.nested(node.orelse))]
         if isinstance(node, ast.Pass):
             return []
         self.fail(node, f"Unsupported statement {type(node).__name__}")
@@ -633,10 +695,28 @@ class _Reader:
         return a
 
     def alloc_var(self, name, call):
-        dtype = str(self.static(call.args[0])) if call.args else "float32"
-        a = Alloc(name, "var", (1,), canonical_dtype(dtype))
+        """``T.alloc_var(dtype, init=0)``: a mutable per-thread scalar (python/ntilang/frontend.py:916-965)."""
+        kw = {k.arg: k.value for k in call.keywords}
+        args = list(call.args)
+        if args:
+            dtype_node = args.pop(0)
+        elif "dtype" in kw:
+            dtype_node = kw["dtype"]
+        else:
+            self.fail(call, "alloc_var requires dtype")
+        dtype = canonical_dtype(str(self.static(dtype_node)))
+        init = kw.get("init", args[0] if args else None)
+        if init is not None:
+            ok, v = self.try_static(init)
+            value = Const(v) if ok and v is None else self.expr(init)
+            if isinstance(value, Const) and value.value is None:
+                value = Const(0)
+        else:
+            value = Const(0)
+        a = Alloc(name, "var", (1,), dtype)
         self.buffers[name] = a
-        return a
+        self.mutables[name] = dtype
+        return [a, Let(name, Call("cast", (simplify(value), Const(dtype))))]
 
     def for_stmt(self, node):
         it = node.iter
@@ -648,7 +728,7 @@ class _Reader:
             saved = self.in_parallel
             self.in_parallel = True
             self.kernel_names.update(tnames)
-            body = self.block(node.body)
+            body = self.nested(node.body)
             self.in_parallel = saved
             return [Parallel(tuple(tnames), extents, body)]
         if name in ("Pipelined", "serial", "Serial", "unroll", "Unroll", "range", "grid"):
@@ -660,7 +740,8 @@ class _Reader:
             if name == "grid":
                 if len(tnames) != len(args):
                     self.fail(node, "T.grid target count must match its extents")
-                stmts = self.block(node.body)
+                self.kernel_names.update(tnames)
+                stmts = self.nested(node.body)
                 for var, ext in reversed(list(zip(tnames, args))):
                     stmts = [Loop(var, Const(0), simplify(self.expr(ext)), "serial", 0, stmts)]
                 self.kernel_names.update(tnames)
@@ -671,7 +752,7 @@ class _Reader:
             start = start if isinstance(start, Const) else simplify(self.expr(start))
             stop = simplify(self.expr(stop))
             self.kernel_names.add(tnames[0])
-            body = self.block(node.body)
+            body = self.nested(node.body)
             kind = "pipelined" if name == "Pipelined" else "serial"
             return [Loop(tnames[0], start, stop, kind, stages, body)]
         self.fail(node, "Loops must iterate T.Parallel, T.Pipelined, T.serial, T.grid or range")
@@ -722,6 +803,13 @@ class _Reader:
             if not -rank <= dim < rank:
                 self.fail(call, "Scan dimension is outside the source rank")
             return [Scan("sum" if name.startswith("cumsum") else "max", src, dst, dim % rank, reverse)]
+        if name in _ATOMICS:
+            dst = arg(0, "dst")
+            if not isinstance(dst, ast.Subscript):
+                self.fail(call, f"T.{name} needs an element destination")
+            buf = self.buffer_name(dst.value)
+            idx = tuple(self.index_list(dst.slice))
+            return [Atomic(_ATOMICS[name], buf, idx, simplify(self.expr(arg(1, "value"))))]
         if name in ("use_swizzle", "annotate_layout", "print", "device_assert", "Assert"):
             return [Hint(name)]
         self.fail(call, f"Unsupported kernel statement T.{name}")
@@ -739,7 +827,9 @@ _CMPOPS = {
     ast.GtE: lambda a, b: a >= b, ast.Eq: lambda a, b: a == b, ast.NotEq: lambda a, b: a != b,
 }
 _CMPSYM = {ast.Lt: "<", ast.LtE: "<=", ast.Gt: ">", ast.GtE: ">=", ast.Eq: "==", ast.NotEq: "!="}
-_DTYPE_CALLS = ("float32", "float16", "bfloat16", "int32", "float64")
+_DTYPE_CALLS = {n: n for n in ("float32", "float16", "bfloat16", "float64", "int8", "int16", "int32", "int64",
+                                "uint8", "uint16", "uint32", "uint64", "bool")}
+_DTYPE_CALLS.update({"half": "float16", "float": "float32", "double": "float64", "int": "int32", "long": "int64"})
 
 
 # ------------------------------------------------------------------------ simplification
@@ -833,7 +923,7 @@ def read_program(program: PrimFunc) -> Program:
 
 
 __all__ = [
-    "Alloc", "Bin", "Call", "Cmp", "Const", "Copy", "Fill", "Gemm", "Hint", "If", "Let", "Load",
+    "Alloc", "Atomic", "Bin", "Call", "Cmp", "Const", "Copy", "Fill", "Gemm", "Hint", "If", "Let", "Load",
     "Loop", "Parallel", "Program", "Reduce", "Region", "Scan", "Select", "Store", "Var", "affine",
     "read_program", "simplify",
 ]

@@ -39,55 +39,80 @@ def gemm_workspace(device, nbytes: int):
     return buf
 
 
-def _size(value, tensor, dim):
-    """Static size from the spec, or the bound value of a symbolic dimension."""
-    return int(tensor.shape[dim]) if isinstance(value, str) else int(value)
+def abi_call(spec: OpSpec):
+    """(C-ABI entry point, argument recipe) of a recognised op.
 
-
-def launch(spec: OpSpec, tensors, stream: int) -> None:
-    f = spec.family
-    p = spec.params
-    a = spec.args
+    A recipe item is ``("ptr", i)`` (argument i's data pointer), ``("null",)``, ``("i32", v)``,
+    ``("i64", v)``, ``("f32", v)``, ``("dim", i, d)`` (argument i's size along d, int64),
+    ``("rows", i)`` (product of argument i's sizes but the last) or ``("stream",)``.  The same
+    recipe drives ``launch`` and the standalone module ``CompiledKernel.save()`` writes.
+    """
+    f, p, a = spec.family, spec.params, spec.args
     if f == "elementwise":
-        x, y, out = tensors[a["a"]], tensors[a["b"]], tensors[a["c"]]
-        n = _size(p["count"], out, 0)
-        _lib.call("ntl_binary_f32", _BINARY_OPS[p["op"]], _ptr(x), _ptr(y), _ptr(out), n, stream)
-    elif f == "cumsum":
-        x, y = tensors[a["x"]], tensors[a["y"]]
-        rows = x.numel() // x.shape[-1] if x.dim() > 1 else 1
-        cols = int(x.shape[-1])
-        _lib.call("ntl_cumsum_f32", _ptr(x), _ptr(y), rows, cols, int(p["reverse"]), stream)
-    elif f == "softmax":
-        x, y = tensors[a["x"]], tensors[a["y"]]
-        _lib.call("ntl_softmax_f32", _ptr(x), _ptr(y), int(x.shape[0]), int(x.shape[1]), stream)
-    elif f == "rmsnorm":
-        x, w, y = tensors[a["x"]], tensors[a["w"]], tensors[a["y"]]
-        _lib.call("ntl_rmsnorm_f32", _ptr(x), _ptr(w), _ptr(y), int(x.shape[0]), int(x.shape[1]),
-                  float(p["eps"]), float(p["inv_n"]), stream)
-    elif f == "layernorm":
-        x, w, b, y = tensors[a["x"]], tensors[a["w"]], tensors[a["b"]], tensors[a["y"]]
-        _lib.call("ntl_layernorm_f32", _ptr(x), _ptr(w), _ptr(b), _ptr(y), int(x.shape[0]), int(x.shape[1]),
-                  float(p["eps"]), float(p["inv_n"]), stream)
-    elif f == "transpose":
-        src, dst = tensors[a["a"]], tensors[a["b"]]
-        _lib.call("ntl_transpose_f32", _ptr(src), _ptr(dst), int(src.shape[0]), int(src.shape[1]), stream)
-    elif f == "gemm":
-        A, B, C = tensors[a["a"]], tensors[a["b"]], tensors[a["c"]]
-        bias = tensors[a["bias"]] if "bias" in a else None
-        M, K = int(A.shape[0]), int(A.shape[1])
-        N = int(B.shape[0]) if p["transpose_b"] else int(B.shape[1])
+        count = ("dim", a["c"], 0) if isinstance(p["count"], str) else ("i64", int(p["count"]))
+        return "ntl_binary_f32", [("i32", _BINARY_OPS[p["op"]]), ("ptr", a["a"]), ("ptr", a["b"]), ("ptr", a["c"]),
+                                  count, ("stream",)]
+    if f == "cumsum":
+        return "ntl_cumsum_f32", [("ptr", a["x"]), ("ptr", a["y"]), ("rows", a["x"]), ("dim", a["x"], -1),
+                                  ("i32", int(p["reverse"])), ("stream",)]
+    if f == "softmax":
+        return "ntl_softmax_f32", [("ptr", a["x"]), ("ptr", a["y"]), ("dim", a["x"], 0), ("dim", a["x"], 1),
+                                   ("stream",)]
+    if f == "rmsnorm":
+        return "ntl_rmsnorm_f32", [("ptr", a["x"]), ("ptr", a["w"]), ("ptr", a["y"]), ("dim", a["x"], 0),
+                                   ("dim", a["x"], 1), ("f32", float(p["eps"])), ("f32", float(p["inv_n"])),
+                                   ("stream",)]
+    if f == "layernorm":
+        return "ntl_layernorm_f32", [("ptr", a["x"]), ("ptr", a["w"]), ("ptr", a["b"]), ("ptr", a["y"]),
+                                     ("dim", a["x"], 0), ("dim", a["x"], 1), ("f32", float(p["eps"])),
+                                     ("f32", float(p["inv_n"])), ("stream",)]
+    if f == "transpose":
+        return "ntl_transpose_f32", [("ptr", a["a"]), ("ptr", a["b"]), ("dim", a["a"], 0), ("dim", a["a"], 1),
+                                     ("stream",)]
+    if f == "gemm":
         # Data-parallel tiles: on B200 splitting the last wave along K (ntl_gemm_f16_f32_ws)
         # measured no faster at any shape tried; the partial-sum fixup costs about what the
         # idle part of the wave does.
-        _lib.call("ntl_gemm_f16_f32", _ptr(A), _ptr(B), _ptr(C), _ptr(bias) if bias is not None else None,
-                  int(p["bias_mode"]), float(p["alpha"]), int(p["relu"]), M, N, K, int(p["transpose_b"]), stream)
-    elif f == "fa2":
-        q, k, v, o = tensors[a["q"]], tensors[a["k"]], tensors[a["v"]], tensors[a["o"]]
-        b, h, s, d = (int(x) for x in q.shape)
-        _lib.call("ntl_fa2_fwd_f16", _ptr(q), _ptr(k), _ptr(v), _ptr(o), b, h, s, d, float(p["scale_log2"]),
-                  int(p["causal"]), stream)
-    else:  # pragma: no cover - recognize() only produces the families above
-        raise RuntimeError(f"no launcher for op family {f!r}")
+        tb = int(p["transpose_b"])
+        return "ntl_gemm_f16_f32", [("ptr", a["a"]), ("ptr", a["b"]), ("ptr", a["c"]),
+                                    ("ptr", a["bias"]) if "bias" in a else ("null",), ("i32", int(p["bias_mode"])),
+                                    ("f32", float(p["alpha"])), ("i32", int(p["relu"])), ("dim", a["a"], 0),
+                                    ("dim", a["b"], 0 if tb else 1), ("dim", a["a"], 1), ("i32", tb), ("stream",)]
+    if f == "fa2":
+        return "ntl_fa2_fwd_f16", [("ptr", a["q"]), ("ptr", a["k"]), ("ptr", a["v"]), ("ptr", a["o"]),
+                                   ("dim", a["q"], 0), ("dim", a["q"], 1), ("dim", a["q"], 2), ("dim", a["q"], 3),
+                                   ("f32", float(p["scale_log2"])), ("i32", int(p["causal"])), ("stream",)]
+    raise RuntimeError(f"no C-ABI call for op family {f!r}")  # pragma: no cover
+
+
+def _recipe_args(recipe, tensors, stream):
+    out = []
+    for item in recipe:
+        kind = item[0]
+        if kind == "ptr":
+            out.append(_ptr(tensors[item[1]]))
+        elif kind == "null":
+            out.append(None)
+        elif kind in ("i32", "i64", "f32"):
+            out.append(item[1])
+        elif kind == "dim":
+            out.append(int(tensors[item[1]].shape[item[2]]))
+        elif kind == "rows":
+            t = tensors[item[1]]
+            out.append(t.numel() // t.shape[-1] if t.dim() > 1 else 1)
+        elif kind == "stream":
+            out.append(stream)
+        else:  # pragma: no cover - recipes come from abi_call
+            raise RuntimeError(f"bad recipe item {item!r}")
+    return out
+
+
+def launch(spec: OpSpec, tensors, stream: int, bindings=None) -> None:
+    if spec.family == "pointwise":
+        spec.params["kernel"].launch(tensors, bindings or {}, stream)
+        return
+    entry, recipe = abi_call(spec)
+    _lib.call(entry, *_recipe_args(recipe, tensors, stream))
 
 
 ABI_CALL = {
@@ -99,15 +124,17 @@ ABI_CALL = {
     "transpose": "ntl_transpose_f32(A, B, m, n, stream)",
     "gemm": "ntl_gemm_f16_f32(A, B, C, bias, bias_mode, alpha, relu, M, N, K, b_trans, stream)",
     "fa2": "ntl_fa2_fwd_f16(Q, K, V, O, batch, heads, seq, dim, scale_log2, causal, stream)",
+    "pointwise": "ntl_rtc_build(cuda_source, name, &handle) once, then ntl_rtc_launch(handle, grid, 256, args, stream)",
 }
 
 
 def describe(spec: OpSpec, name: str, target: str) -> str:
-    """The text ``CompiledKernel.source`` returns: what will be launched and how."""
+    """The launch plan: what will be launched and how (comment lines)."""
+    params = {k: v for k, v in spec.params.items() if k != "kernel"}
     lines = [
         f"# ntilang_b200 launch plan for kernel `{name}` (target {target})",
         f"# op family : {spec.family}",
-        f"# parameters: {', '.join(f'{k}={v}' for k, v in spec.params.items())}",
+        f"# parameters: {', '.join(f'{k}={v}' for k, v in params.items())}",
         f"# arguments : {', '.join(f'{k}=arg{v}' for k, v in spec.args.items())}",
         f"# C ABI     : {ABI_CALL[spec.family]}  (libntl_kernels.so, include/ntl_kernels.h)",
     ]

@@ -145,7 +145,7 @@ def _fold(e):
     """Light algebraic clean-up on symbolic row/epilogue expressions."""
     if isinstance(e, Call):
         args = tuple(_fold(a) for a in e.args)
-        if e.fn == "max" and len(args) == 2 and isinstance(args[1], Const) and args[1].value == -math.inf:
+        if e.fn in ("max", "maximum") and len(args) == 2 and isinstance(args[1], Const) and args[1].value == -math.inf:
             return args[0]
         if e.fn == "neg" and isinstance(args[0], Const):
             return Const(-args[0].value)
@@ -808,7 +808,7 @@ class Epilogue:
         """result -> (alpha, (bias_mode, bias_name) | None, relu)."""
         e = _fold(self.result)
         relu = False
-        if isinstance(e, Call) and e.fn == "max" and len(e.args) == 2:
+        if isinstance(e, Call) and e.fn in ("max", "maximum") and len(e.args) == 2:
             a, b = e.args
             if isinstance(a, Const):
                 a, b = b, a

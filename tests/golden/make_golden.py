@@ -166,6 +166,42 @@ def main():
         scale = (1.0 / np.sqrt(64)) * 1.44269504
         save(f"fa2_1x2x128x64_{'causal' if causal else 'full'}", q=q, k=k, v=v, o=o, scale_log2=np.array(scale),
              causal=np.array(causal))
+
+    # Generic elementwise programs (the NVRTC path): the reference's own examples, then the
+    # shared programs of pw_programs.py built under the reference package.
+    fa_ex = load_example(ref, "fragment_affine")
+    rng = np.random.default_rng(31)
+    a = np.concatenate([np.linspace(-2, 2, 129, dtype=np.float32), rng.normal(size=128).astype(np.float32)])
+    b = np.full_like(a, np.nan)
+    reference(fa_ex.fragment_affine(), a, b)
+    save("pw_fragment_affine_257", a=a, b=b)
+    pw_ex = load_example(ref, "piecewise")
+    a = np.concatenate([np.linspace(-2, 2, 61, dtype=np.float32), np.array([-0.0, 0.0, 1.0, -1.0], np.float32),
+                        np.random.default_rng(32).normal(size=28).astype(np.float32) * 3])
+    b = np.full_like(a, np.nan)
+    reference(pw_ex.piecewise(), a, b)
+    save("pw_piecewise_93", a=a, b=b)
+    ws_ex = load_example(ref, "window_sum")
+    a = np.random.default_rng(33).normal(size=(7, 3, 5)).astype(np.float32)
+    windows = ((-1, 5), (0, 0), (2, 4), (10, 10), (3, 2))
+    outs = []
+    for rows, columns in windows:
+        b = np.full(7, np.nan, np.float32)
+        reference(ws_ex.window_sum(), a, b, rows, columns)
+        outs.append(b)
+    save("pw_window_sum_7x3x5", a=a, b=np.stack(outs), windows=np.array(windows, np.int32))
+    sys.path.insert(0, str(HERE))
+    import pw_programs
+    import ntilang.language as T_ref
+
+    for name, (factory, build, outs_idx, scalars) in pw_programs.PROGRAMS.items():
+        if not wanted(f"pw_{name}"):
+            continue
+        arrays = build(np.random.default_rng(40 + sorted(pw_programs.PROGRAMS).index(name)))
+        inputs = [x.copy() for x in arrays]
+        reference(factory(T_ref, ntilang.compile), *arrays, *scalars)
+        save(f"pw_{name}", **{f"in{i}": x for i, x in enumerate(inputs)}, **{f"out{i}": arrays[i] for i in outs_idx},
+             scalars=np.array(scalars, np.float64))
     print(f"done in {time.time() - t0:.1f} s")
 
 

@@ -154,8 +154,21 @@ def test_unsupported_program_raises_compile_error():
             for i in T.Parallel(256):
                 D[bx * 256 + i] = A[bx * 256 + i] * B[bx * 256 + i] + C[bx * 256 + i]
 
-    with pytest.raises(CompileError, match="not one of the op families"):
-        ntilang.compile(fused_multiply_add)
+    # Not a recognised family: it runs on the generic elementwise (NVRTC) path.
+    kern = ntilang.compile(fused_multiply_add)
+    assert kern.spec.family == "pointwise"
+    assert "ntl_pw_fused_multiply_add" in kern.get_kernel_source()
+
+    @T.prim_func
+    def shifted_fragment(A: T.Tensor((64,), "float32"), B: T.Tensor((64,), "float32")):
+        with T.Kernel(1, threads=64):
+            tile = T.alloc_fragment((64,), "float32")
+            T.copy(A, tile)
+            for i in T.Parallel(63):
+                B[i] = tile[i + 1]
+
+    with pytest.raises(CompileError, match="not one of the op families(.|\n)*pointwise: .*slot mapping"):
+        ntilang.compile(shifted_fragment)
 
 
 def test_transpose_with_store_load_form_is_recognised():
