@@ -303,6 +303,51 @@ class VaddOp(RowOp):
         return n * 3 * m * 4 / dt / 1e9, f"{n} x vector add [{m}]"
 
 
+class GenericFmaOp(RowOp):
+    """A program outside the recognised families: CUDA C generated per program, NVRTC-compiled."""
+
+    name = "pointwise"
+    n = 16 * 1024 * 1024
+    config = "generic elementwise D = A*B + C (separately rounded), A,B,C f32 [16777216] ~N(0,1), NVRTC path"
+
+    def setup(self):
+        import ntilang
+        import ntilang.language as T
+
+        n, block = self.n, 1024
+
+        @T.prim_func
+        def generic_fma(A: T.Tensor((n,), "float32"), B: T.Tensor((n,), "float32"), C: T.Tensor((n,), "float32"),
+                        D: T.Tensor((n,), "float32")):
+            with T.Kernel(T.ceildiv(n, block), threads=256) as b:
+                for k in T.Parallel(block):
+                    D[b * block + k] = A[b * block + k] * B[b * block + k] + C[b * block + k]
+
+        self.kernel = ntilang.compile(generic_fma, out_idx=[-1])
+        assert self.kernel.spec.family == "pointwise"
+        k = self.sets_needed(4 * self.n * 4)
+        self.sets = []
+        for s in range(k):
+            a, b, c = (self.gen((self.n,), 1.0, 1000 * self.rank + 3 * s + j) for j in range(3))
+            d = self.torch.empty_like(a)
+            self.sets.append(((a, b, c, d), (a, b, c), d))
+
+    def units(self):
+        return 4 * self.n * 4
+
+    def cpu(self, seconds):
+        import numpy as np
+
+        m = 4 * 1024 * 1024
+        a, b, c = (np.random.default_rng(j).normal(size=m).astype(np.float32) for j in range(3))
+        n, t0 = 0, time.perf_counter()
+        while time.perf_counter() - t0 < seconds:
+            np.add(np.multiply(a, b), c)
+            n += 1
+        dt = time.perf_counter() - t0
+        return n * 4 * m * 4 / dt / 1e9, f"{n} x numpy a*b+c [{m}] (float32, separately rounded)"
+
+
 class GemmOp(Op):
     name = "gemm"
     bound = "tensor"
@@ -418,7 +463,7 @@ class FA2CausalOp(FA2Op):
 
 
 OPS = {c.name: c for c in (CumsumOp, RMSNormOp, SoftmaxOp, VaddOp, GemmOp, GemmBiasReluOp, FA2Op, FA2CausalOp,
-                           LayerNormOp, TransposeOp)}
+                           LayerNormOp, TransposeOp, GenericFmaOp)}
 
 
 # ------------------------------------------------------------------------------ clocks

@@ -14,6 +14,7 @@ legacy stream).  It performs no argument checks: it is the launch, not the drop-
 from __future__ import annotations
 
 from .launch import abi_call, describe
+from .pointwise import BLOCK_THREADS, POINTS_PER_THREAD
 
 _RUNTIME = r'''
 import ctypes
@@ -127,7 +128,7 @@ class _Kernel:
         keep += [ctypes.c_int64(extents[i]) for i in GRID_ARGS]
         keep.append(ctypes.c_int64(total))
         argv = (ctypes.c_void_p * len(keep))(*[ctypes.cast(ctypes.pointer(k), ctypes.c_void_p) for k in keep])
-        grid = (total + BLOCK - 1) // BLOCK
+        grid = (total + BLOCK * UNROLL - 1) // (BLOCK * UNROLL)
         _check(self.lib, self.lib.ntl_rtc_launch(ctypes.c_uint64(self.handle), ctypes.c_uint64(grid),
                                                  ctypes.c_uint32(BLOCK), argv, ctypes.c_void_p(int(stream))),
                "ntl_rtc_launch")
@@ -185,7 +186,8 @@ def standalone_module(spec, prog, name: str, target: str, library: str | None) -
             f"GRID = {tuple(_grid_literal(g) for g in k.grid)!r}",
             f"GRID_ARGS = {tuple(k.grid_args)!r}",
             f"POINTS = {k.points}",
-            "BLOCK = 256",
+            f"BLOCK = {BLOCK_THREADS}",
+            f"UNROLL = {POINTS_PER_THREAD}",
             "CUDA_SOURCE = r'''",
             k.source.replace("'''", "' ' '"),
             "'''",
