@@ -63,6 +63,12 @@ int ntl_binary_f32(int op, const float* a, const float* b, float* c, int64_t n, 
  * (scan.py:168-237, evaluate :349-389), so results are bit-identical to it. */
 int ntl_cumsum_f32(const float* x, float* y, int64_t rows, int64_t cols, int reverse, ntl_stream_t stream);
 
+/* Inclusive prefix maximum along each row (T.cummax), same layout and reverse flag as
+ * ntl_cumsum_f32.  Replaces the FFI call of the scan emitted for T.cummax
+ * (python/ntilang/scan.py:83-115, examples/scan.py:7-21): identity -inf, combine fmax
+ * (a NaN operand is ignored, +0 orders above -0; scan.py:26-29, :366-374). */
+int ntl_cummax_f32(const float* x, float* y, int64_t rows, int64_t cols, int reverse, ntl_stream_t stream);
+
 /* Row softmax y = exp(x - max) / sum(exp(x - max)) over [rows, cols] fp32.  Replaces the
  * FFI call of the row-reduction kernel emitted for examples/softmax.py:9-25
  * (codegen.py:1028-1240).  Sums follow the reference's balanced tree over the row padded

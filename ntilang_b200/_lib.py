@@ -25,6 +25,7 @@ SIGNATURES = {
     "ntl_vadd_f32": (ctypes.c_int, [c_f32p, c_f32p, c_f32p, c_i64, ctypes.c_void_p]),
     "ntl_binary_f32": (ctypes.c_int, [ctypes.c_int, c_f32p, c_f32p, c_f32p, c_i64, ctypes.c_void_p]),
     "ntl_cumsum_f32": (ctypes.c_int, [c_f32p, c_f32p, c_i64, c_i64, ctypes.c_int, ctypes.c_void_p]),
+    "ntl_cummax_f32": (ctypes.c_int, [c_f32p, c_f32p, c_i64, c_i64, ctypes.c_int, ctypes.c_void_p]),
     "ntl_softmax_f32": (ctypes.c_int, [c_f32p, c_f32p, c_i64, c_i64, ctypes.c_void_p]),
     "ntl_rmsnorm_f32": (ctypes.c_int, [c_f32p, c_f32p, c_f32p, c_i64, c_i64, ctypes.c_float, ctypes.c_float,
                                        ctypes.c_void_p]),

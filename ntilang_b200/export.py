@@ -13,7 +13,7 @@ legacy stream).  It performs no argument checks: it is the launch, not the drop-
 
 from __future__ import annotations
 
-from .launch import abi_call, describe
+from .launch import abi_calls, describe
 from .pointwise import BLOCK_THREADS, POINTS_PER_THREAD
 
 _RUNTIME = r'''
@@ -43,12 +43,20 @@ class _Kernel:
 
     def __init__(self, lib):
         self.lib = lib
-        self.fn = getattr(lib, ENTRY)
-        self.fn.restype = ctypes.c_int
+        self.calls = []
+        for entry, recipe in CALLS:
+            fn = getattr(lib, entry)
+            fn.restype = ctypes.c_int
+            self.calls.append((entry, fn, recipe))
 
     def __call__(self, *args, stream=0):
+        for entry, fn, recipe in self.calls:
+            _check(self.lib, fn(*self._values(recipe, args, stream)), entry)
+
+    @staticmethod
+    def _values(recipe, args, stream):
         values = []
-        for item in RECIPE:
+        for item in recipe:
             kind = item[0]
             if kind == "ptr":
                 a = args[item[1]]
@@ -67,7 +75,7 @@ class _Kernel:
                 values.append(ctypes.c_int64(rows))
             else:  # stream
                 values.append(ctypes.c_void_p(int(stream)))
-        _check(self.lib, self.fn(*values), ENTRY)
+        return values
 
 
 def compile_kernel(library=None):
@@ -194,8 +202,8 @@ def standalone_module(spec, prog, name: str, target: str, library: str | None) -
             _RTC_KERNEL.strip("\n"),
         ]
     else:
-        entry, recipe = abi_call(spec)
-        body += [f"ENTRY = {entry!r}", f"RECIPE = {tuple(tuple(r) for r in recipe)!r}", _ABI_KERNEL.strip("\n")]
+        calls = tuple((entry, tuple(tuple(r) for r in recipe)) for entry, recipe in abi_calls(spec))
+        body += [f"CALLS = {calls!r}", _ABI_KERNEL.strip("\n")]
     return "\n".join(head + [""] + body) + "\n"
 
 

@@ -41,6 +41,38 @@ def cumsum(rows, cols, reverse=False, rows_per_block=4):
 
 
 @jit(out_idx=[-1])
+def cummax(rows, cols, reverse=False, rows_per_block=4):
+    @T.prim_func
+    def row_running_max(X: T.Tensor((rows, cols), "float32"), Y: T.Tensor((rows, cols), "float32")):
+        with T.Kernel(T.ceildiv(rows, rows_per_block), threads=128) as b:
+            buf = T.alloc_fragment((rows_per_block, cols), "float32")
+            T.copy(X[b * rows_per_block : (b + 1) * rows_per_block, :], buf)
+            T.cummax(buf, dim=1, reverse=reverse)
+            T.copy(buf, Y[b * rows_per_block : (b + 1) * rows_per_block, :])
+
+    return row_running_max
+
+
+@jit(out_idx=[1, 2])
+def sum_and_max_scans(rows, cols, reverse=False, rows_per_block=4):
+    """Prefix sums and prefix maxima of one loaded tile (the shape of examples/scan.py)."""
+
+    @T.prim_func
+    def two_scans(X: T.Tensor((rows, cols), "float32"), Sums: T.Tensor((rows, cols), "float32"),
+                  Maxima: T.Tensor((rows, cols), "float32")):
+        with T.Kernel(T.ceildiv(rows, rows_per_block), threads=128) as b:
+            loaded = T.alloc_fragment((rows_per_block, cols), "float32")
+            sums = T.alloc_fragment((rows_per_block, cols), "float32")
+            T.copy(X[b * rows_per_block : (b + 1) * rows_per_block, :], loaded)
+            T.cumsum(loaded, sums, dim=1, reverse=reverse)
+            T.cummax(loaded, dim=1, reverse=reverse)
+            T.copy(sums, Sums[b * rows_per_block : (b + 1) * rows_per_block, :])
+            T.copy(loaded, Maxima[b * rows_per_block : (b + 1) * rows_per_block, :])
+
+    return two_scans
+
+
+@jit(out_idx=[-1])
 def softmax(rows, cols, rows_per_block=4):
     width = 1 << max(0, (cols - 1).bit_length())
     ninf = -T.infinity("float32")
@@ -282,5 +314,5 @@ def flash_attention(batch, heads, seq_len, dim, is_causal=False, block_m=128, bl
     return attention
 
 
-__all__ = ["cumsum", "flash_attention", "layernorm", "matmul", "matmul_bias_relu", "matmul_scaled_bias_relu", "rmsnorm",
-           "softmax", "transpose", "vector_add"]
+__all__ = ["cummax", "cumsum", "flash_attention", "layernorm", "matmul", "matmul_bias_relu", "matmul_scaled_bias_relu", "rmsnorm",
+           "softmax", "sum_and_max_scans", "transpose", "vector_add"]

@@ -52,9 +52,9 @@ def abi_call(spec: OpSpec):
         count = ("dim", a["c"], 0) if isinstance(p["count"], str) else ("i64", int(p["count"]))
         return "ntl_binary_f32", [("i32", _BINARY_OPS[p["op"]]), ("ptr", a["a"]), ("ptr", a["b"]), ("ptr", a["c"]),
                                   count, ("stream",)]
-    if f == "cumsum":
-        return "ntl_cumsum_f32", [("ptr", a["x"]), ("ptr", a["y"]), ("rows", a["x"]), ("dim", a["x"], -1),
-                                  ("i32", int(p["reverse"])), ("stream",)]
+    if f in ("cumsum", "cummax"):
+        return f"ntl_{f}_f32", [("ptr", a["x"]), ("ptr", a["y"]), ("rows", a["x"]), ("dim", a["x"], -1),
+                                ("i32", int(p["reverse"])), ("stream",)]
     if f == "softmax":
         return "ntl_softmax_f32", [("ptr", a["x"]), ("ptr", a["y"]), ("dim", a["x"], 0), ("dim", a["x"], 1),
                                    ("stream",)]
@@ -85,6 +85,18 @@ def abi_call(spec: OpSpec):
     raise RuntimeError(f"no C-ABI call for op family {f!r}")  # pragma: no cover
 
 
+def abi_calls(spec: OpSpec):
+    """Every C-ABI call of a recognised op, in launch order: one per family, one per scan for a
+    kernel with several row scans of one tile (examples/scan.py)."""
+    if spec.family == "scans":
+        a = spec.args
+        return [(f"ntl_{'cumsum' if kind == 'sum' else 'cummax'}_f32",
+                 [("ptr", a["x"]), ("ptr", a[f"y{i}"]), ("rows", a["x"]), ("dim", a["x"], -1), ("i32", int(rev)),
+                  ("stream",)])
+                for i, (kind, rev) in enumerate(spec.params["scans"])]
+    return [abi_call(spec)]
+
+
 def _recipe_args(recipe, tensors, stream):
     out = []
     for item in recipe:
@@ -111,13 +123,15 @@ def launch(spec: OpSpec, tensors, stream: int, bindings=None) -> None:
     if spec.family == "pointwise":
         spec.params["kernel"].launch(tensors, bindings or {}, stream)
         return
-    entry, recipe = abi_call(spec)
-    _lib.call(entry, *_recipe_args(recipe, tensors, stream))
+    for entry, recipe in abi_calls(spec):
+        _lib.call(entry, *_recipe_args(recipe, tensors, stream))
 
 
 ABI_CALL = {
     "elementwise": "ntl_binary_f32(op, A, B, C, n, stream)",
     "cumsum": "ntl_cumsum_f32(X, Y, rows, cols, reverse, stream)",
+    "cummax": "ntl_cummax_f32(X, Y, rows, cols, reverse, stream)",
+    "scans": "ntl_cumsum_f32 / ntl_cummax_f32(X, Y_i, rows, cols, reverse_i, stream), one per output",
     "softmax": "ntl_softmax_f32(X, Y, rows, cols, stream)",
     "rmsnorm": "ntl_rmsnorm_f32(X, W, Y, rows, cols, eps, inv_n, stream)",
     "layernorm": "ntl_layernorm_f32(X, W, B, Y, rows, cols, eps, inv_n, stream)",

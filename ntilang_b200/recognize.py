@@ -574,33 +574,51 @@ def _match_elementwise(prog: Program) -> OpSpec:
 
 
 def _match_cumsum(prog: Program) -> OpSpec:
+    """Row scans: one load copy of a parameter into a tile, T.cumsum / T.cummax calls on that
+    loaded tile (in place or into another tile), and store copies of the scanned tiles
+    (examples/cumsum.py:7-14, examples/scan.py:7-21)."""
     body = _body(prog.body)
     scans = [s for s in body if isinstance(s, Scan)]
-    need(len(scans) == 1, "one T.cumsum")
-    sc = scans[0]
-    need(sc.kind == "sum", "cumsum")
+    need(len(scans) >= 1, "one T.cumsum")
     need(len(prog.grid) == 1, "row scans use a 1-D grid")
     bx = prog.block_vars[0]
-    idx = body.index(sc)
-    pre, post = body[:idx], body[idx + 1:]
+    first = body.index(scans[0])
+    pre = body[:first]
     need(len(pre) == 1 and isinstance(pre[0], Copy), "one load copy before the scan")
-    need(len(post) == 1 and isinstance(post[0], Copy), "one store copy after the scan")
-    load, store = pre[0], post[0]
+    load = pre[0]
     src_param, tile = load.src.buf, load.dst.buf
     need(_is_param(prog, src_param) and not _is_param(prog, tile), "load copies a parameter into a tile")
-    need(sc.src.buf == tile, "scan reads the loaded tile")
     tshape = prog.buffers[tile].shape
-    need(tuple(sc.src.extents) == tuple(tshape) and tuple(sc.dst.extents) == tuple(tshape),
-         "scan covers the whole tile")
-    need(all(_aff_is(s, {}) for s in sc.src.starts + sc.dst.starts), "scan covers the whole tile")
-    need(sc.dim == len(tshape) - 1, "scans run along the last dimension")
-    need(store.src.buf == sc.dst.buf and _is_param(prog, store.dst.buf), "store copies the scanned tile out")
-    dst_param = store.dst.buf
+    content = {tile: None}  # tile -> None (the loaded rows) or (kind, reverse)
+    stores = []
+    for s in body[first:]:
+        if isinstance(s, Scan):
+            need(s.src.buf in content and content[s.src.buf] is None, "scan reads the loaded tile")
+            need(tuple(s.src.extents) == tuple(tshape) and tuple(s.dst.extents) == tuple(tshape),
+                 "scan covers the whole tile")
+            need(all(_aff_is(x, {}) for x in s.src.starts + s.dst.starts), "scan covers the whole tile")
+            need(s.dim == len(tshape) - 1, "scans run along the last dimension")
+            need(prog.buffers[s.dst.buf].dtype == "float32" and prog.buffers[s.dst.buf].shape == tshape,
+                 "float32 scan tiles of one shape")
+            content[s.dst.buf] = (s.kind, bool(s.reverse))
+        elif isinstance(s, Copy):
+            need(s.src.buf in content and content[s.src.buf] is not None and _is_param(prog, s.dst.buf),
+                 "store copies the scanned tile out")
+            stores.append((s, content[s.src.buf]))
+        else:
+            raise NoMatch(f"unsupported {type(s).__name__} in a scan kernel")
+    need(stores, "store copies the scanned tile out")
     pshape = prog.buffers[src_param].shape
-    need(prog.buffers[dst_param].shape == pshape, "input and output shapes match")
-    need(prog.buffers[src_param].dtype == "float32" and prog.buffers[dst_param].dtype == "float32",
+    outs = []
+    for st, (kind, rev) in stores:
+        dst_param = st.dst.buf
+        need(prog.buffers[dst_param].shape == pshape, "input and output shapes match")
+        need(prog.buffers[dst_param].dtype == "float32", "cumsum kernels are float32")
+        need(dst_param != src_param, "in-place scans are not supported")
+        outs.append((kind, rev, dst_param))
+    need(prog.buffers[src_param].dtype == "float32" and prog.buffers[tile].dtype == "float32",
          "cumsum kernels are float32")
-    need(prog.buffers[tile].dtype == "float32", "float32 scan tile")
+    need(len({d for _, _, d in outs}) == len(outs), "each output written once")
     if len(pshape) == 1:
         need(tshape == pshape and _grid_extent(prog, bx) == 1, "1-D scans take the whole vector")
         rows, cols = 1, _dim(pshape[0])
@@ -608,16 +626,20 @@ def _match_cumsum(prog: Program) -> OpSpec:
         need(len(pshape) == 2 and len(tshape) == 2, "2-D row scans")
         rb, cols = tshape[0], pshape[1]
         need(tshape[1] == cols, "tile width equals the row length")
-        for region in (load.src, store.dst):
+        for region in [load.src] + [st.dst for st, _ in stores]:
             need(_aff_is(region.starts[0], {bx: rb}) or (_grid_extent(prog, bx) == 1 and _aff_is(region.starts[0], {})),
                  "copies move rows bx*rows .. +rows")
             need(_aff_is(region.starts[1], {}), "copies move whole rows")
             need(region.point or region.extents[0] in (rb, None), "copy row extent equals the tile rows")
         need(_covers(prog, bx, rb, pshape[0]), "grid must cover every row")
         rows, cols = _dim(pshape[0]), _dim(cols)
-    need(src_param != dst_param, "in-place scans are not supported")
-    return OpSpec("cumsum", {"rows": rows, "cols": cols, "reverse": bool(sc.reverse)},
-                  {"x": _param_index(prog, src_param), "y": _param_index(prog, dst_param)})
+    x = _param_index(prog, src_param)
+    if len(outs) == 1:
+        kind, rev, dst = outs[0]
+        family = "cumsum" if kind == "sum" else "cummax"
+        return OpSpec(family, {"rows": rows, "cols": cols, "reverse": rev}, {"x": x, "y": _param_index(prog, dst)})
+    return OpSpec("scans", {"rows": rows, "cols": cols, "scans": tuple((k, r) for k, r, _ in outs)},
+                  {"x": x, **{f"y{i}": _param_index(prog, d) for i, (_, _, d) in enumerate(outs)}})
 
 
 # ----------------------------------------------------------------------------------- GEMM
@@ -951,7 +973,7 @@ def recognize(prog: Program) -> OpSpec:
             reasons.append(f"{name}: {type(exc).__name__} {exc}")
     raise CompileError(
         f"{prog.name}: program is not one of the op families implemented by the sm_100a kernels "
-        "(elementwise, cumsum, softmax, rmsnorm, layernorm, transpose, gemm, fa2):\n  " + "\n  ".join(reasons)
+        "(elementwise, cumsum / cummax, softmax, rmsnorm, layernorm, transpose, gemm, fa2):\n  " + "\n  ".join(reasons)
     )
 
 

@@ -10,6 +10,7 @@ performs, in the reference's operation order where the order changes the result:
 * ``vadd``            examples/vector_add.py:5-10 (one fp32 add per element)
 * ``cumsum_rows``     python/ntilang/scan.py:349-389 (``evaluate``: 32-column Hillis-Steele
                       segments, sequential carry from +0) == the device order of scan.py:132-240
+* ``cummax_rows``     the same DAG with fmax and identity -inf (scan.py:26-29, :366-374)
 * ``softmax_rows``    examples/softmax.py:9-25 with the reduction tree of codegen.py:1094-1151
 * ``rmsnorm_rows``    examples/rmsnorm.py:13-37 with the same tree
 * ``gemm``            python/ntilang/testing.py:356-360 (fp32 product of upcast fp16), with the
@@ -64,6 +65,39 @@ def cumsum_rows(x: np.ndarray, reverse: bool = False) -> np.ndarray:
         order = range(seg.shape[1] - 1, -1, -1) if reverse else range(seg.shape[1])
         for s in order:
             seg[:, s, :] = seg[:, s, :] + carry[:, None]
+            carry = seg[:, s, 0 if reverse else 31].copy()
+    return work[:, :n].reshape(shape).copy()
+
+
+def _fmax_pos_zero(left, right):
+    """np.fmax with +0 above -0 (scan.py:366-374: fmaxf ignores NaN and prefers +0)."""
+    out = np.fmax(left, right)
+    zero = np.where(np.signbit(left) & np.signbit(right), np.float32(-0.0), np.float32(0.0))
+    return np.where((left == 0) & (right == 0), zero, out).astype(np.float32)
+
+
+def cummax_rows(x: np.ndarray, reverse: bool = False) -> np.ndarray:
+    """Inclusive prefix maximum along the last axis in the reference's segment order
+    (scan.py:349-389 with kind "max": identity -inf, combine fmax)."""
+    x = np.asarray(x, dtype=np.float32)
+    shape = x.shape
+    rows = x.reshape(-1, shape[-1]) if x.ndim > 1 else x.reshape(1, -1)
+    n = rows.shape[1]
+    padded = (n + 31) // 32 * 32
+    work = np.full((rows.shape[0], padded), -np.inf, dtype=np.float32)
+    work[:, :n] = rows
+    seg = work.reshape(rows.shape[0], padded // 32, 32)
+    with np.errstate(invalid="ignore"):
+        for o in (1, 2, 4, 8, 16):
+            old = seg.copy()
+            if reverse:
+                seg[..., :-o] = _fmax_pos_zero(old[..., :-o], old[..., o:])
+            else:
+                seg[..., o:] = _fmax_pos_zero(old[..., o:], old[..., :-o])
+        carry = np.full(rows.shape[0], -np.inf, dtype=np.float32)
+        order = range(seg.shape[1] - 1, -1, -1) if reverse else range(seg.shape[1])
+        for s in order:
+            seg[:, s, :] = _fmax_pos_zero(seg[:, s, :], carry[:, None])
             carry = seg[:, s, 0 if reverse else 31].copy()
     return work[:, :n].reshape(shape).copy()
 

@@ -167,6 +167,23 @@ def main():
         save(f"fa2_1x2x128x64_{'causal' if causal else 'full'}", q=q, k=k, v=v, o=o, scale_log2=np.array(scale),
              causal=np.array(causal))
 
+    # Row sum and maximum scans of one tile (examples/scan.py), forward and reverse, with
+    # signed zeros, infinities and NaN in some rows.
+    sc_ex = load_example(ref, "scan")
+    rng = np.random.default_rng(51)
+    x = rng.normal(size=(9, 113)).astype(np.float32)
+    x[2, 10:20] = 0.0
+    x[2, 12] = -0.0
+    x[3, :] = -0.0
+    x[4, 5] = np.nan
+    x[5, 40] = np.inf
+    x[6, 7] = -np.inf
+    for rev in (False, True):
+        prefix = np.full_like(x, np.nan)
+        maximum = np.full_like(x, np.nan)
+        reference(sc_ex.scan(9, 113, reverse=rev), x, prefix, maximum)
+        save(f"scan_9x113_{'rev' if rev else 'fwd'}", x=x, prefix=prefix, maximum=maximum, reverse=np.array(rev))
+
     # Generic elementwise programs (the NVRTC path): the reference's own examples, then the
     # shared programs of pw_programs.py built under the reference package.
     fa_ex = load_example(ref, "fragment_affine")

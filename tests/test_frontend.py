@@ -312,6 +312,8 @@ def test_reference_examples_are_recognised():
         ("vector_add", ()): "elementwise", ("cumsum", ()): "cumsum", ("softmax", ()): "softmax",
         ("rmsnorm", ()): "rmsnorm", ("matmul", ()): "gemm", ("matmul_relu", ()): "gemm",
         ("flash_attention", ()): "fa2", ("layernorm", ()): "layernorm", ("transpose", ()): "transpose",
+        ("scan", ()): "scans", ("fragment_affine", ()): "pointwise", ("piecewise", ()): "pointwise",
+        ("window_sum", ()): "pointwise",
     }
     for (name, args), family in expect.items():
         kern = getattr(load(name), name)(*args)

@@ -117,6 +117,35 @@ def test_cumsum_baseline_size_bit_exact(torch_cuda, reverse):
     assert ok, f"{bad} elements differ"
 
 
+@pytest.mark.parametrize("case", ["scan_9x113_fwd", "scan_9x113_rev"])
+def test_sum_and_max_scans_golden_bit_exact(torch_cuda, case):
+    """examples/scan.py's two outputs (cumsum and cummax of one tile) against the reference
+    evaluator, through the factory with the same program shape."""
+    torch = torch_cuda
+    g = golden(case)
+    rows, cols = g["x"].shape
+    kern = K.sum_and_max_scans(rows, cols, bool(g["reverse"]))
+    assert kern.spec.family == "scans"
+    sums, maxima = kern(to_gpu(torch, g["x"]))
+    for got, want in ((sums, g["prefix"]), (maxima, g["maximum"])):
+        ok, bad = bits_equal(got.cpu().numpy(), want)
+        assert ok, f"{bad} elements differ"
+
+
+@pytest.mark.parametrize("rows,cols", [(1, 1), (3, 2), (2, 31), (9, 33), (3, 129), (6, 1000), (2, 1025),
+                                       (3, 4097), (2, 70001)])
+@pytest.mark.parametrize("reverse", [False, True])
+def test_cummax_ragged_bit_exact(torch_cuda, rows, cols, reverse):
+    torch = torch_cuda
+    rng = np.random.default_rng(rows * 131 + cols)
+    x = rng.normal(size=(rows, cols)).astype(np.float32)
+    x[:, ::17] = 0.0
+    x[:, ::23] = -0.0
+    y = K.cummax(rows, cols, reverse)(to_gpu(torch, x)).cpu().numpy()
+    ok, bad = bits_equal(y, O.cummax_rows(x, reverse))
+    assert ok, f"{bad} elements differ"
+
+
 def test_cumsum_1d_program(torch_cuda):
     """A rank-1 tile scan (one row) written directly with ntilang.compile."""
     torch = torch_cuda

@@ -46,6 +46,19 @@ def test_cumsum_bit_exact(case):
         assert_bits(rowops.cumsum(g["x"], rev), g["y"])
 
 
+@pytest.mark.parametrize("case", ["scan_9x113_fwd", "scan_9x113_rev"])
+def test_sum_and_max_scans_bit_exact(case):
+    """examples/scan.py (T.cumsum into a second tile, T.cummax in place) with signed zeros,
+    infinities and a NaN, from the reference evaluator."""
+    g = golden(case)
+    rev = bool(g["reverse"])
+    with np.errstate(over="ignore", invalid="ignore"):
+        assert_bits(O.cumsum_rows(g["x"], rev), g["prefix"])
+    assert_bits(O.cummax_rows(g["x"], rev), g["maximum"])
+    zeros = g["maximum"][3]  # an all -0 row stays -0; a row mixing signed zeros rises to +0
+    assert np.all(np.signbit(zeros))
+
+
 def test_cumsum_order_differs_from_sequential():
     """The reference's segment order is not a sequential prefix sum: torch/np.cumsum is no oracle."""
     g = golden("cumsum_eval_64x1000_fwd")

@@ -237,7 +237,7 @@ def test_saved_module_is_standalone(tmp_path):
     from ntilang_b200 import kernels as K
 
     fam = K.vector_add(1024)
-    assert _imports(fam.source) == {"ctypes", "os"} and "ENTRY = 'ntl_binary_f32'" in fam.source
+    assert _imports(fam.source) == {"ctypes", "os"} and "CALLS = (('ntl_binary_f32'" in fam.source
 
 
 @needs_nvrtc
