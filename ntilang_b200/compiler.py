@@ -59,14 +59,19 @@ class CompiledKernel:
         return hashlib.sha256(self.source.encode("utf-8")).hexdigest()
 
     def get_kernel_source(self) -> str:
-        """Device code: the generated CUDA C for a generic elementwise program, else the launch
+        """The standalone launcher module (``source``), as the reference returns its generated
+        module here (python/ntilang/compiler.py:36-42)."""
+        return self.source
+
+    def get_host_source(self) -> str:
+        return self.source
+
+    def get_cuda_source(self) -> str:
+        """Device code: the generated CUDA C of a generic elementwise program, else the launch
         plan of the prebuilt sm_100a kernel in libntl_kernels.so."""
         if self.spec is not None and self.spec.family == "pointwise":
             return self.spec.params["kernel"].source
         return describe(self.spec, self.ir.name, self.target)
-
-    def get_host_source(self) -> str:
-        return self.source
 
     def save(self, path) -> Path:
         """Write the standalone launcher module (python/ntilang/compiler.py:44-49)."""

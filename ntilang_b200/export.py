@@ -5,7 +5,7 @@ The reference exports the generated CuTe DSL module, which runs wherever CuTe ru
 device code is libntl_kernels.so (prebuilt sm_100a kernels plus the NVRTC path), so the
 exported module is plain Python over ``ctypes``: it imports nothing from ``ntilang`` /
 ``ntilang_b200``, finds the library through ``$NTL_KERNELS_LIB`` or the path recorded when it
-was saved, and its ``compile_kernel()`` returns a callable taking the kernel's arguments in
+was saved, and its ``compile_kernel()`` returns a callable (``run(...)`` launches directly) taking the kernel's arguments in
 prim_func order (objects with ``data_ptr()`` and ``shape``, e.g. torch CUDA tensors, for
 tensors; Python numbers for scalars) plus ``stream=`` (a CUDA stream handle, default the
 legacy stream).  It performs no argument checks: it is the launch, not the drop-in wrapper.
@@ -23,8 +23,8 @@ import os
 _C = {"i32": ctypes.c_int, "i64": ctypes.c_int64, "f32": ctypes.c_float}
 
 
-def _library(path=None):
-    path = path or os.environ.get("NTL_KERNELS_LIB") or LIBRARY
+def _library():
+    path = os.environ.get("NTL_KERNELS_LIB") or LIBRARY
     if not path or not os.path.exists(path):
         raise RuntimeError("libntl_kernels.so not found: set NTL_KERNELS_LIB")
     return ctypes.CDLL(path)
@@ -78,9 +78,19 @@ class _Kernel:
         return values
 
 
-def compile_kernel(library=None):
+def compile_kernel():
     """Load libntl_kernels.so and return the launch callable."""
-    return _Kernel(_library(library))
+    return _Kernel(_library())
+
+
+_CACHED = []
+
+
+def run(*args, stream=0):
+    """Launch with the kernel's arguments (compile_kernel() on first use)."""
+    if not _CACHED:
+        _CACHED.append(compile_kernel())
+    _CACHED[0](*args, stream=stream)
 '''
 
 _RTC_KERNEL = r'''
@@ -142,9 +152,19 @@ class _Kernel:
                "ntl_rtc_launch")
 
 
-def compile_kernel(library=None):
+def compile_kernel():
     """Load libntl_kernels.so, compile the CUDA source with NVRTC and return the launch callable."""
-    return _Kernel(_library(library))
+    return _Kernel(_library())
+
+
+_CACHED = []
+
+
+def run(*args, stream=0):
+    """Launch with the kernel's arguments (compile_kernel() on first use)."""
+    if not _CACHED:
+        _CACHED.append(compile_kernel())
+    _CACHED[0](*args, stream=stream)
 '''
 
 
