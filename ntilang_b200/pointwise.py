@@ -41,8 +41,8 @@ from dataclasses import dataclass, field
 
 from . import _lib
 from .frontend import (Alloc, Atomic, Bin, Call, Cmp, Const, Copy, Fill, Gemm, Hint, If, Let, Load, Loop, Parallel,
-                       Program, Reduce, Region, Scan, Select, Store, Var)
-from .ir import DTYPES, CompileError, ScalarParameter, SymDim, TensorParameter, integer_limits
+                       Program, Reduce, Scan, Select, Store, Var)
+from .ir import DTYPES, CompileError, ScalarParameter, SymDim, integer_limits
 
 BLOCK_THREADS = 256
 # Points per thread: a CTA covers POINTS_PER_THREAD consecutive runs of BLOCK_THREADS points
@@ -144,11 +144,6 @@ def _c_literal(value, dtype: str) -> str:
     return str(v) if v != -(2**31) else "(-2147483647 - 1)"
 
 
-def _is_param_buf(prog: Program, name: str) -> bool:
-    p = prog.param(name)
-    return isinstance(p, TensorParameter)
-
-
 @dataclass
 class PointwiseKernel:
     """A lowered program: CUDA C source plus what the host needs to launch it."""
@@ -228,6 +223,8 @@ class _Lowering:
         self.fragments: dict = {}  # fragment name -> shape
         self.mutable_scope: dict = {}  # alloc_var name -> parallel nesting level at declaration
         self.parallel_level = 0
+        self.guards: list = []  # open `pt < n` guards (collective copies / fills)
+        self.current_parallel = None  # the T.Parallel loop being lowered
         self.points = 1
         self.sym_names = tuple(s.name for s in prog.sym_dims)
         for p in prog.params:
@@ -495,8 +492,6 @@ class _Lowering:
             self.fail(f"fragment {name} must be accessed at the coordinates of a T.Parallel loop of its shape "
                       f"{tuple(shape)} (the per-thread slot mapping)")
 
-    current_parallel = None
-
     # ------------------------------------------------------------- statements
     def stmts(self, body):
         for s in body:
@@ -587,22 +582,22 @@ class _Lowering:
         self.fail(f"unsupported statement {type(s).__name__}")
 
     class _PointsGuard:
+        """`if (pt < n) { ... }`: the statements run for the first n points of a block instance."""
+
         def __init__(self, low, n):
             self.low, self.n = low, n
 
         def __enter__(self):
             low = self.low
             low.points = max(low.points, self.n)
-            low._guards.append(self.n)
+            low.guards.append(self.n)
             low.emit(f"if (pt < {self.n}LL) {{")
             low.depth += 1
 
         def __exit__(self, *exc):
             self.low.depth -= 1
             self.low.emit("}")
-            self.low._guards.pop()
-
-    _guards: list = []
+            self.low.guards.pop()
 
     def _points(self, n):
         return self._PointsGuard(self, n)
@@ -662,7 +657,7 @@ class _Lowering:
             val = f"ntl_f2b({val})"
         line = f"p_{_ident(name)}[{self.offset(name, codes)}] = {val};"
         guard = pred
-        if self.current_parallel is None and not self._guards:
+        if self.current_parallel is None and not self.guards:
             guard = f"pt == 0" + (f" && {pred}" if pred else "")  # one writer per block instance
         self.emit(f"if ({guard}) {line}" if guard else line)
 
@@ -680,7 +675,7 @@ class _Lowering:
         fn = {"add": "atomicAdd", "max": "atomicMax", "min": "atomicMin"}[s.op]
         line = f"{fn}(&p_{_ident(s.buf)}[{self.offset(s.buf, codes)}], {self.conv(code, d, b.dtype)});"
         guard = pred
-        if self.current_parallel is None and not self._guards:
+        if self.current_parallel is None and not self.guards:
             guard = "pt == 0" + (f" && {pred}" if pred else "")
         self.emit(f"if ({guard}) {line}" if guard else line)
 
@@ -782,7 +777,6 @@ def _ident(name: str) -> str:
 def lower(prog: Program) -> PointwiseKernel:
     """Lower ``prog`` to CUDA C or raise ``CompileError`` when it is not elementwise."""
     low = _Lowering(prog)
-    low._guards = []
     low.depth = 2
     low.stmts(prog.body)
     body = low.lines

@@ -16,7 +16,6 @@ produced by the reference's own evaluator, pin it.  Only ``tests/`` may import t
 
 from __future__ import annotations
 
-import math
 
 import numpy as np
 
