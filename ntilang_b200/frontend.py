@@ -215,6 +215,8 @@ _MATH_FUNCS = {
     "ceil": "ceil", "trunc": "trunc", "round": "round", "nearbyint": "nearbyint", "isnan": "isnan",
     "isinf": "isinf", "isfinite": "isfinite", "pow": "pow", "fmod": "fmod", "clamp": "clamp",
     "floordiv": "//", "floormod": "%", "truncdiv": "truncdiv", "truncmod": "truncmod",
+    "bitwise_and": "&", "bitwise_or": "|", "bitwise_xor": "^", "shift_left": "<<", "shift_right": ">>",
+    "bitwise_not": "invert",
 }
 _ATOMICS = {"atomic_add": "add", "atomic_max": "max", "atomic_min": "min"}
 
@@ -417,6 +419,8 @@ class _Reader:
                 return self.expr(node.operand)
             if isinstance(node.op, ast.Not):
                 return Call("not", (self.expr(node.operand),))
+            if isinstance(node.op, ast.Invert):
+                return Call("invert", (self.expr(node.operand),))
             self.fail(node, "Unsupported unary operator")
         if isinstance(node, ast.Compare) and len(node.ops) == 1:
             return Cmp(_CMPSYM[type(node.ops[0])], self.expr(node.left), self.expr(node.comparators[0]))
@@ -450,7 +454,7 @@ class _Reader:
                 return Call("min", (Call("max", (args[0], args[1])), args[2]))
             if name in _MATH_FUNCS:
                 fn = _MATH_FUNCS[name]
-                if fn in ("//", "%"):
+                if fn in ("//", "%", "&", "|", "^", "<<", ">>"):
                     return Bin(fn, *args)
                 return Call(fn, tuple(args))
             if name in _DTYPE_CALLS:
@@ -821,7 +825,8 @@ _BINOPS = {
     ast.Pow: lambda a, b: a**b, ast.LShift: lambda a, b: a << b, ast.RShift: lambda a, b: a >> b,
     ast.BitAnd: lambda a, b: a & b, ast.BitOr: lambda a, b: a | b, ast.BitXor: lambda a, b: a ^ b,
 }
-_BINSYM = {ast.Add: "+", ast.Sub: "-", ast.Mult: "*", ast.Div: "/", ast.FloorDiv: "//", ast.Mod: "%"}
+_BINSYM = {ast.Add: "+", ast.Sub: "-", ast.Mult: "*", ast.Div: "/", ast.FloorDiv: "//", ast.Mod: "%",
+           ast.BitAnd: "&", ast.BitOr: "|", ast.BitXor: "^", ast.LShift: "<<", ast.RShift: ">>"}
 _CMPOPS = {
     ast.Lt: lambda a, b: a < b, ast.LtE: lambda a, b: a <= b, ast.Gt: lambda a, b: a > b,
     ast.GtE: lambda a, b: a >= b, ast.Eq: lambda a, b: a == b, ast.NotEq: lambda a, b: a != b,
@@ -842,7 +847,7 @@ def simplify(e):
         if isinstance(a, Const) and isinstance(b, Const):
             try:
                 return Const(_PYOP[e.op](a.value, b.value))
-            except ZeroDivisionError:
+            except (ZeroDivisionError, TypeError, ValueError):
                 return Bin(e.op, a, b)
         if e.op in ("+", "-", "*"):
             fa, fb = affine(a), affine(b)
@@ -866,7 +871,9 @@ def simplify(e):
 
 
 _PYOP = {"+": lambda a, b: a + b, "-": lambda a, b: a - b, "*": lambda a, b: a * b,
-         "/": lambda a, b: a / b, "//": lambda a, b: a // b, "%": lambda a, b: a % b}
+         "/": lambda a, b: a / b, "//": lambda a, b: a // b, "%": lambda a, b: a % b,
+         "&": lambda a, b: a & b, "|": lambda a, b: a | b, "^": lambda a, b: a ^ b,
+         "<<": lambda a, b: a << b, ">>": lambda a, b: a >> b}
 
 
 def affine(e):

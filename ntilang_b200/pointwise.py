@@ -353,6 +353,8 @@ class _Lowering:
 
     def binary(self, e):
         (a, da), (b, db) = self.expr(e.a), self.expr(e.b)
+        if e.op in ("&", "|", "^", "<<", ">>"):
+            return self.bitwise(e.op, e.a, e.b, a, da, b, db)
         d = promote(da, db)
         if d == "bool":
             self.fail(f"arithmetic operator {e.op!r} on two Boolean operands")
@@ -376,8 +378,45 @@ class _Lowering:
         u = UNSIGNED[d]
         return f"(({CTYPE[d]})(({u})({ca}) {op} ({u})({cb})))", d
 
+    def bitwise(self, op, ea, eb, a, da, b, db):
+        """& | ^ << >> on integers / Booleans; an int literal takes the other operand's integer
+        dtype when it fits (python/ntilang/scalar.py:81-96)."""
+        for d in (da, db):
+            if d in FLOATS:
+                self.fail("Bitwise operations require integer or Boolean operands")
+        lit_a = isinstance(ea, Const) and type(ea.value) is int
+        lit_b = isinstance(eb, Const) and type(eb.value) is int
+        if lit_a != lit_b:
+            lit, other = (ea, db) if lit_a else (eb, da)
+            if other in CTYPE and other not in FLOATS:
+                low, high = integer_limits(other)
+                if not low <= lit.value <= high:
+                    self.fail(f"Bitwise integer literal must fit the other operand's {other} dtype")
+                if lit_a:
+                    da = other
+                else:
+                    db = other
+        d = promote(da, db)
+        if op in ("<<", ">>"):
+            if "bool" in (da, db):
+                self.fail("Shift operations require integer operands, excluding Boolean")
+            x, y = self.conv(a, da, d), self.conv(b, db, d)
+            if op == "<<":
+                return f"(({CTYPE[d]})(({UNSIGNED[d]})({x}) << (unsigned)({y})))", d
+            return f"(({CTYPE[d]})(({x}) >> (unsigned)({y})))", d
+        if d == "bool":
+            return f"({a} {op} {b})", "bool"
+        return f"(({CTYPE[d]})({self.conv(a, da, d)} {op} {self.conv(b, db, d)}))", d
+
     def call(self, e):
         fn = e.fn
+        if fn == "invert":
+            a, da = self.expr(e.args[0])
+            if da in FLOATS:
+                self.fail("Bitwise operations require integer or Boolean operands")
+            if da == "bool":
+                return f"(!{a})", "bool"
+            return f"(({CTYPE[da]})(~({a})))", da
         if fn == "cast":
             (a, da) = self.expr(e.args[0])
             target = e.args[1].value if len(e.args) > 1 else "float32"

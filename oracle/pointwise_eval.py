@@ -105,6 +105,8 @@ class _Eval:
         if k == "Cmp":
             return "bool"
         if k == "Bin":
+            if e.op in ("&", "|", "^", "<<", ">>"):
+                return promote(*self._bit_operand_dtypes(e))
             return promote(self.dtype(e.a), self.dtype(e.b))
         if k == "Select":
             return promote(self.dtype(e.a), self.dtype(e.b))
@@ -126,6 +128,17 @@ class _Eval:
             return d
         raise TypeError(k)
 
+    def _bit_operand_dtypes(self, e):
+        """An int literal takes the other operand's integer dtype (scalar.py:81-96)."""
+        da, db = self.dtype(e.a), self.dtype(e.b)
+        lit_a = type(e.a).__name__ == "Const" and type(e.a.value) is int
+        lit_b = type(e.b).__name__ == "Const" and type(e.b.value) is int
+        if lit_a and not lit_b and db not in _FLOATS:
+            da = db
+        elif lit_b and not lit_a and da not in _FLOATS:
+            db = da
+        return da, db
+
     def buf_dtype(self, name):
         b = self.prog.buffers[name]
         return b.dtype
@@ -144,6 +157,17 @@ class _Eval:
             d = promote(self.dtype(e.a), self.dtype(e.b))
             a, b = cast(self.ev(e.a), d), cast(self.ev(e.b), d)
             return bool({"<": a < b, "<=": a <= b, ">": a > b, ">=": a >= b, "==": a == b, "!=": a != b}[e.op])
+        if k == "Bin" and e.op in ("&", "|", "^", "<<", ">>"):
+            da, db = self._bit_operand_dtypes(e)
+            d = promote(da, db)
+            a, b = cast(self.ev(e.a), d), cast(self.ev(e.b), d)
+            with np.errstate(all="ignore"):
+                if d == "bool":
+                    r = {"&": a & b, "|": a | b, "^": a ^ b}[e.op]
+                else:
+                    r = {"&": lambda: a & b, "|": lambda: a | b, "^": lambda: a ^ b,
+                         "<<": lambda: a << b, ">>": lambda: a >> b}[e.op]()
+            return cast(r, d)
         if k == "Bin":
             d = promote(self.dtype(e.a), self.dtype(e.b))
             a, b = self.ev(e.a), self.ev(e.b)
@@ -171,6 +195,10 @@ class _Eval:
             return bool(self.ev(e.args[0])) or bool(self.ev(e.args[1]))
         if fn == "not":
             return not bool(self.ev(e.args[0]))
+        if fn == "invert":
+            d = self.dtype(e.args[0])
+            v = cast(self.ev(e.args[0]), d)
+            return (not bool(v)) if d == "bool" else cast(~v, d)
         d = self.dtype(e)
         vals = [self.ev(a) for a in e.args]
         if fn in ("max", "min", "maximum", "minimum"):

@@ -4,7 +4,8 @@ Each factory takes the ``T`` module and the ``compile`` function of the package 
 it: ``make_golden.py`` builds them under the reference package to produce golden vectors with
 its evaluator, the tests build them under ``ntilang_b200``.  Together with the reference's own
 examples/fragment_affine.py, piecewise.py and window_sum.py they cover float32 / float16
-arithmetic and promotion, Python-style integer floor division, Boolean logic and selects,
+arithmetic and promotion, Python-style integer floor division, bitwise operators and shifts,
+Boolean logic and selects,
 scalar parameters, 2-D grids with partial tiles, fragment copies and atomics.
 """
 
@@ -88,6 +89,20 @@ def histogram(T, compile):
     return compile(histogram)
 
 
+def bit_mix(T, compile, n=256):
+    @T.prim_func
+    def bit_mix(X: T.Tensor((n,), "int32"), U: T.Tensor((n,), "uint32"), Y: T.Tensor((n,), "int32"),
+                V: T.Tensor((n,), "uint32")):
+        with T.Kernel(T.ceildiv(n, 128), threads=128) as bx:
+            for i in T.Parallel(128):
+                x = X[bx * 128 + i]
+                u = U[bx * 128 + i]
+                Y[bx * 128 + i] = ((x & 255) | (x >> 3)) ^ (~x << 2)
+                V[bx * 128 + i] = ((u >> 5) ^ (u << 7)) | (u & 3855)
+
+    return compile(bit_mix)
+
+
 # name -> (factory, input builder(seed) -> list of arrays in parameter order (outputs NaN / 0 filled),
 #          indices of output arrays, scalar arguments after the arrays)
 def _f32(rng, *shape, scale=1.0):
@@ -104,6 +119,9 @@ PROGRAMS = {
     "select_logic": (select_logic, lambda rng: [_f32(rng, 37, 45, scale=2.0), _f32(rng, 37, 45, scale=2.0),
                                                 np.full((37, 45), np.nan, np.float32)], (2,), ()),
     "tile_copy": (tile_copy, lambda rng: [_f32(rng, 50, 70), np.full((50, 70), np.nan, np.float32)], (1,), ()),
+    "bit_mix": (bit_mix, lambda rng: [rng.integers(-2**31, 2**31 - 1, size=256, dtype=np.int64).astype(np.int32),
+                                      rng.integers(0, 2**32 - 1, size=256, dtype=np.uint64).astype(np.uint32),
+                                      np.zeros(256, np.int32), np.zeros(256, np.uint32)], (2, 3), ()),
     "histogram": (histogram, lambda rng: [rng.integers(-50, 50, size=64).astype(np.int32),
                                           np.zeros(8, np.int32), np.full(8, -1, np.int32)], (1, 2), ()),
 }
