@@ -179,6 +179,22 @@ class If:
 
 
 @dataclass
+class While:
+    cond: object
+    body: list
+
+
+@dataclass
+class Break:
+    pass
+
+
+@dataclass
+class Continue:
+    pass
+
+
+@dataclass
 class Hint:
     kind: str
     args: dict = field(default_factory=dict)
@@ -672,6 +688,14 @@ class _Reader:
             self.fail(node, "Unsupported augmented assignment")
         if isinstance(node, ast.For):
             return self.for_stmt(node)
+        if isinstance(node, ast.While):
+            if node.orelse:
+                self.fail(node, "while ... else is not supported")
+            return [While(simplify(self.expr(node.test)), self.nested(node.body))]
+        if isinstance(node, ast.Break):
+            return [Break()]
+        if isinstance(node, ast.Continue):
+            return [Continue()]
         if isinstance(node, ast.If):
             ok, test = self.try_static(node.test)
             if ok:
@@ -814,6 +838,10 @@ class _Reader:
             buf = self.buffer_name(dst.value)
             idx = tuple(self.index_list(dst.slice))
             return [Atomic(_ATOMICS[name], buf, idx, simplify(self.expr(arg(1, "value"))))]
+        if name in ("loop_break", "break_loop"):
+            return [Break()]
+        if name == "continue_loop":
+            return [Continue()]
         if name in ("use_swizzle", "annotate_layout", "print", "device_assert", "Assert"):
             return [Hint(name)]
         self.fail(call, f"Unsupported kernel statement T.{name}")
@@ -930,7 +958,8 @@ def read_program(program: PrimFunc) -> Program:
 
 
 __all__ = [
-    "Alloc", "Atomic", "Bin", "Call", "Cmp", "Const", "Copy", "Fill", "Gemm", "Hint", "If", "Let", "Load",
-    "Loop", "Parallel", "Program", "Reduce", "Region", "Scan", "Select", "Store", "Var", "affine",
+    "Alloc", "Atomic", "Bin", "Break", "Call", "Cmp", "Const", "Continue", "Copy", "Fill", "Gemm", "Hint", "If",
+    "Let", "Load",
+    "Loop", "Parallel", "Program", "Reduce", "Region", "Scan", "Select", "Store", "Var", "While", "affine",
     "read_program", "simplify",
 ]

@@ -40,8 +40,8 @@ import re
 from dataclasses import dataclass, field
 
 from . import _lib
-from .frontend import (Alloc, Atomic, Bin, Call, Cmp, Const, Copy, Fill, Gemm, Hint, If, Let, Load, Loop, Parallel,
-                       Program, Reduce, Scan, Select, Store, Var)
+from .frontend import (Alloc, Atomic, Bin, Break, Call, Cmp, Const, Continue, Copy, Fill, Gemm, Hint, If, Let, Load,
+                       Loop, Parallel, Program, Reduce, Scan, Select, Store, Var, While)
 from .ir import DTYPES, CompileError, ScalarParameter, SymDim, integer_limits
 
 BLOCK_THREADS = 256
@@ -224,6 +224,7 @@ class _Lowering:
         self.mutable_scope: dict = {}  # alloc_var name -> parallel nesting level at declaration
         self.parallel_level = 0
         self.guards: list = []  # open `pt < n` guards (collective copies / fills)
+        self.loops: list = []  # enclosing loops, innermost last: "serial" (a program loop) or "parallel"
         self.current_parallel = None  # the T.Parallel loop being lowered
         self.points = 1
         self.sym_names = tuple(s.name for s in prog.sym_dims)
@@ -564,11 +565,31 @@ class _Lowering:
             lo, hi = self.interval(s.start), self.interval(s.stop)
             if lo is not None and hi is not None:
                 self.ranges[s.var] = (lo[0], hi[1] - 1)
-            self.emit(f"for ({CTYPE[d]} v_{v} = {self.conv(a, da, d)}; v_{v} < {self.conv(b, db, d)}; ++v_{v}) {{")
+            # The bound is evaluated once, before the first iteration (a Python range).
+            self.emit(f"for ({CTYPE[d]} v_{v} = {self.conv(a, da, d)}, e_{v} = {self.conv(b, db, d)}; v_{v} < e_{v}; "
+                      f"++v_{v}) {{")
             self.depth += 1
+            self.loops.append("serial")
             self.stmts(s.body)
+            self.loops.pop()
             self.depth -= 1
             self.emit("}")
+            return
+        if isinstance(s, While):
+            c, dc = self.expr(s.cond)
+            self.emit(f"while ({self.conv(c, dc, 'bool')}) {{")
+            self.depth += 1
+            self.loops.append("serial")
+            self.stmts(s.body)
+            self.loops.pop()
+            self.depth -= 1
+            self.emit("}")
+            return
+        if isinstance(s, (Break, Continue)):
+            if not self.loops or self.loops[-1] != "serial":
+                self.fail("break / continue must be inside a serial loop (T.serial, T.grid, range, while), "
+                          "not directly in T.Parallel")
+            self.emit("break;" if isinstance(s, Break) else "continue;")
             return
         if isinstance(s, If):
             c, dc = self.expr(s.cond)
@@ -672,7 +693,9 @@ class _Lowering:
                 self.emit(f"const int v_{_ident(v)} = {code};")
             self.current_parallel = s
             self.parallel_level += 1
+            self.loops.append("parallel")
             self.stmts(s.body)
+            self.loops.pop()
             self.parallel_level -= 1
             self.current_parallel = None
         self.ranges = saved

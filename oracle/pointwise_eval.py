@@ -73,6 +73,14 @@ _UNARY = {"exp": np.exp, "exp2": np.exp2, "log": np.log, "log2": np.log2, "log10
           "rsqrt": lambda v: 1 / np.sqrt(v), "exp10": lambda v: np.power(v.dtype.type(10), v)}
 
 
+class _Break(Exception):
+    pass
+
+
+class _Continue(Exception):
+    pass
+
+
 class _Eval:
     def __init__(self, prog, arrays, scalars):
         self.prog = prog
@@ -273,12 +281,29 @@ class _Eval:
                 self.stmts(s.body)
         elif k == "Loop":
             d = promote(promote(self.dtype(s.start), self.dtype(s.stop)), "int32")
-            v = int(self.ev(s.start))
+            v, stop = int(self.ev(s.start)), int(self.ev(s.stop))  # range(start, stop): bound read once
             self.types[s.var] = d
-            while v < int(self.ev(s.stop)):
+            while v < stop:
                 self.vars[s.var] = cast(v, d)
-                self.stmts(s.body)
+                try:
+                    self.stmts(s.body)
+                except _Continue:
+                    pass
+                except _Break:
+                    break
                 v += 1
+        elif k == "While":
+            while self.ev(s.cond):
+                try:
+                    self.stmts(s.body)
+                except _Continue:
+                    continue
+                except _Break:
+                    break
+        elif k == "Break":
+            raise _Break()
+        elif k == "Continue":
+            raise _Continue()
         elif k == "If":
             self.stmts(s.then if self.ev(s.cond) else s.orelse)
         elif k == "Let":

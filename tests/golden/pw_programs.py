@@ -5,7 +5,7 @@ it: ``make_golden.py`` builds them under the reference package to produce golden
 its evaluator, the tests build them under ``ntilang_b200``.  Together with the reference's own
 examples/fragment_affine.py, piecewise.py and window_sum.py they cover float32 / float16
 arithmetic and promotion, Python-style integer floor division, bitwise operators and shifts,
-Boolean logic and selects,
+Boolean logic and selects, while loops, break and continue,
 scalar parameters, 2-D grids with partial tiles, fragment copies and atomics.
 """
 
@@ -103,6 +103,32 @@ def bit_mix(T, compile, n=256):
     return compile(bit_mix)
 
 
+def lane_loops(T, compile, n=90):
+    """Per-point while loops with lane-dependent trip counts, and a serial loop with
+    continue / break whose exit depends on the data."""
+
+    @T.prim_func
+    def lane_loops(X: T.Tensor((n,), "int32"), Tri: T.Tensor((n,), "int32"), Acc: T.Tensor((n,), "int32")):
+        with T.Kernel(T.ceildiv(n, 32), threads=32) as bx:
+            for i in T.Parallel(32):
+                left = T.alloc_var("int32", X[bx * 32 + i])
+                tri = T.alloc_var("int32", 0)
+                while left > 0:
+                    tri += left
+                    left -= 1
+                Tri[bx * 32 + i] = tri
+                acc = T.alloc_var("int32", 0)
+                for k in T.serial(24):
+                    if k % 3 == 1:
+                        continue
+                    if acc > X[bx * 32 + i] * 4:
+                        break
+                    acc += k
+                Acc[bx * 32 + i] = acc
+
+    return compile(lane_loops)
+
+
 # name -> (factory, input builder(seed) -> list of arrays in parameter order (outputs NaN / 0 filled),
 #          indices of output arrays, scalar arguments after the arrays)
 def _f32(rng, *shape, scale=1.0):
@@ -122,6 +148,8 @@ PROGRAMS = {
     "bit_mix": (bit_mix, lambda rng: [rng.integers(-2**31, 2**31 - 1, size=256, dtype=np.int64).astype(np.int32),
                                       rng.integers(0, 2**32 - 1, size=256, dtype=np.uint64).astype(np.uint32),
                                       np.zeros(256, np.int32), np.zeros(256, np.uint32)], (2, 3), ()),
+    "lane_loops": (lane_loops, lambda rng: [rng.integers(-5, 30, size=90).astype(np.int32),
+                                            np.zeros(90, np.int32), np.zeros(90, np.int32)], (1, 2), ()),
     "histogram": (histogram, lambda rng: [rng.integers(-50, 50, size=64).astype(np.int32),
                                           np.zeros(8, np.int32), np.full(8, -1, np.int32)], (1, 2), ()),
 }

@@ -331,3 +331,16 @@ def test_example_computations_match_reference_goldens_on_the_oracle():
         b = np.full(7, np.nan, np.float32)
         pointwise_eval.evaluate(kern.ir, [g["a"], b], (int(rows), int(cols)))
         np.testing.assert_array_equal(b, expect)
+
+
+def test_break_directly_in_parallel_is_rejected():
+    @T.prim_func
+    def early_exit(A: T.Tensor((32,), "float32")):
+        with T.Kernel(1, threads=32):
+            for i in T.Parallel(32):
+                if i > 3:
+                    break
+                A[i] = 1.0
+
+    with pytest.raises(CompileError, match="inside a serial loop"):
+        ntilang.compile(early_exit)
