@@ -146,6 +146,7 @@ class Loop:
     kind: str  # serial | pipelined | unroll
     stages: int
     body: list
+    step: object = None  # None: 1
 
 
 @dataclass
@@ -776,13 +777,24 @@ class _Reader:
                 return stmts
             if len(tnames) != 1:
                 self.fail(node, "Serial loops bind a single variable")
+            if not args or len(args) > 3:
+                self.fail(node, "serial loops take (stop), (start, stop) or (start, stop, step)")
             start, stop = (Const(0), args[0]) if len(args) == 1 else (args[0], args[1])
             start = start if isinstance(start, Const) else simplify(self.expr(start))
             stop = simplify(self.expr(stop))
+            step_node = args[2] if len(args) == 3 else kw.get("step")
+            step = None
+            if step_node is not None:
+                step = simplify(self.expr(step_node))
+                if isinstance(step, Const):
+                    if step.value == 0:
+                        self.fail(node, "loop step must not be zero")
+                    if step.value == 1:
+                        step = None
             self.kernel_names.add(tnames[0])
             body = self.nested(node.body)
             kind = "pipelined" if name == "Pipelined" else "serial"
-            return [Loop(tnames[0], start, stop, kind, stages, body)]
+            return [Loop(tnames[0], start, stop, kind, stages, body, step)]
         self.fail(node, "Loops must iterate T.Parallel, T.Pipelined, T.serial, T.grid or range")
 
     def call_stmt(self, call):

@@ -557,17 +557,29 @@ class _Lowering:
             return
         if isinstance(s, Loop):
             (a, da), (b, db) = self.expr(s.start), self.expr(s.stop)
-            if da in FLOATS or db in FLOATS:
+            step = s.step if s.step is not None else Const(1)
+            c, dc = self.expr(step)
+            if da in FLOATS or db in FLOATS or dc in FLOATS:
                 self.fail("loop bounds must be integers")
-            d = promote(promote(da, db), "int32")
+            d = promote(promote(promote(da, db), dc), "int32")
             v = _ident(s.var)
             self.types[s.var] = d
             lo, hi = self.interval(s.start), self.interval(s.stop)
-            if lo is not None and hi is not None:
+            if s.step is None and lo is not None and hi is not None:
                 self.ranges[s.var] = (lo[0], hi[1] - 1)
-            # The bound is evaluated once, before the first iteration (a Python range).
-            self.emit(f"for ({CTYPE[d]} v_{v} = {self.conv(a, da, d)}, e_{v} = {self.conv(b, db, d)}; v_{v} < e_{v}; "
-                      f"++v_{v}) {{")
+            else:
+                self.ranges.pop(s.var, None)
+            # Bounds and step are evaluated once, before the first iteration (a Python range).
+            init = f"{CTYPE[d]} v_{v} = {self.conv(a, da, d)}, e_{v} = {self.conv(b, db, d)}"
+            if s.step is None:
+                head = f"for ({init}; v_{v} < e_{v}; ++v_{v}) {{"
+            elif isinstance(step, Const):
+                cmp = "<" if step.value > 0 else ">"
+                head = f"for ({init}; v_{v} {cmp} e_{v}; v_{v} += {self.conv(c, dc, d)}) {{"
+            else:  # a runtime step: its sign picks the test; 0 runs no iteration
+                head = (f"for ({init}, t_{v} = {self.conv(c, dc, d)}; (t_{v} > 0 && v_{v} < e_{v}) || "
+                        f"(t_{v} < 0 && v_{v} > e_{v}); v_{v} += t_{v}) {{")
+            self.emit(head)
             self.depth += 1
             self.loops.append("serial")
             self.stmts(s.body)

@@ -657,7 +657,7 @@ def _match_gemm(prog: Program) -> OpSpec:
     need(len(loops) <= 1, "one K loop")
     if loops:
         loop = loops[0]
-        need(isinstance(loop.start, Const) and loop.start.value == 0, "K loop starts at 0")
+        need(isinstance(loop.start, Const) and loop.start.value == 0 and loop.step is None, "K loop starts at 0, step 1")
         kbody = _body(loop.body)
         kvar = loop.var
         trips = loop.stop.value if isinstance(loop.stop, Const) else None
@@ -881,6 +881,7 @@ def _match_fa2(prog: Program) -> OpSpec:
     loops = [s for s in body if isinstance(s, Loop)]
     need(len(loops) == 1, "one KV loop")
     loop = loops[0]
+    need(loop.step is None, "KV loop steps by 1")
     lbody = _body(loop.body)
     copies = [s for s in lbody if isinstance(s, Copy) and buf[s.src.buf].scope == "global"]
     need(len(copies) == 2, "KV loop copies K and V tiles")

@@ -281,9 +281,10 @@ class _Eval:
                 self.stmts(s.body)
         elif k == "Loop":
             d = promote(promote(self.dtype(s.start), self.dtype(s.stop)), "int32")
-            v, stop = int(self.ev(s.start)), int(self.ev(s.stop))  # range(start, stop): bound read once
+            v, stop = int(self.ev(s.start)), int(self.ev(s.stop))  # range(start, stop, step): read once
+            step = 1 if getattr(s, "step", None) is None else int(self.ev(s.step))
             self.types[s.var] = d
-            while v < stop:
+            while (step > 0 and v < stop) or (step < 0 and v > stop):
                 self.vars[s.var] = cast(v, d)
                 try:
                     self.stmts(s.body)
@@ -291,7 +292,7 @@ class _Eval:
                     pass
                 except _Break:
                     break
-                v += 1
+                v += step
         elif k == "While":
             while self.ev(s.cond):
                 try:

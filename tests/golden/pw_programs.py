@@ -129,6 +129,26 @@ def lane_loops(T, compile, n=90):
     return compile(lane_loops)
 
 
+def strided_rows(T, compile, rows=37, cols=50):
+    """Serial loops with a start, a positive step and a negative step over each row."""
+
+    @T.prim_func
+    def strided_rows(X: T.Tensor((rows, cols), "float32"), Even: T.Tensor((rows,), "float32"),
+                     Back: T.Tensor((rows,), "float32")):
+        with T.Kernel(T.ceildiv(rows, 16), threads=16) as bx:
+            for r in T.Parallel(16):
+                even = T.alloc_var("float32", 0)
+                back = T.alloc_var("float32", 0)
+                for c in T.serial(1, cols, 2):
+                    even += X[bx * 16 + r, c]
+                for c in T.serial(cols - 1, 0, -3):
+                    back = back * 0.5 + X[bx * 16 + r, c]
+                Even[bx * 16 + r] = even
+                Back[bx * 16 + r] = back
+
+    return compile(strided_rows)
+
+
 # name -> (factory, input builder(seed) -> list of arrays in parameter order (outputs NaN / 0 filled),
 #          indices of output arrays, scalar arguments after the arrays)
 def _f32(rng, *shape, scale=1.0):
@@ -150,6 +170,8 @@ PROGRAMS = {
                                       np.zeros(256, np.int32), np.zeros(256, np.uint32)], (2, 3), ()),
     "lane_loops": (lane_loops, lambda rng: [rng.integers(-5, 30, size=90).astype(np.int32),
                                             np.zeros(90, np.int32), np.zeros(90, np.int32)], (1, 2), ()),
+    "strided_rows": (strided_rows, lambda rng: [_f32(rng, 37, 50), np.full(37, np.nan, np.float32),
+                                                np.full(37, np.nan, np.float32)], (1, 2), ()),
     "histogram": (histogram, lambda rng: [rng.integers(-50, 50, size=64).astype(np.int32),
                                           np.zeros(8, np.int32), np.full(8, -1, np.int32)], (1, 2), ()),
 }
