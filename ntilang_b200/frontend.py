@@ -224,6 +224,8 @@ class NotStatic(Exception):
     pass
 
 
+_LANGUAGE_MODULE = PrimFunc.__module__
+
 _MATH_FUNCS = {
     "exp": "exp", "exp2": "exp2", "__exp": "exp", "log": "log", "log2": "log2", "sqrt": "sqrt",
     "rsqrt": "rsqrt", "abs": "abs", "maximum": "maximum", "max": "max", "minimum": "minimum", "min": "min",
@@ -300,11 +302,20 @@ class _Reader:
         return False
 
     def call_name(self, node):
+        """The T.* (or builtin) name a call refers to.  A bare name bound in the environment to a
+        marker or to ``range`` (``loop = T.serial``, ``stop = T.loop_break``) resolves to it."""
         if isinstance(node, ast.Call):
             f = node.func
             if isinstance(f, ast.Attribute):
                 return f.attr
             if isinstance(f, ast.Name):
+                if f.id not in self.kernel_names and f.id in self.env:
+                    value = self.env[f.id]
+                    if value is builtins.range:
+                        return "range"
+                    marker = getattr(value, "__qualname__", None)
+                    if callable(value) and getattr(value, "__module__", "") == _LANGUAGE_MODULE and marker:
+                        return marker
                 return f.id
         return None
 
@@ -466,9 +477,12 @@ class _Reader:
             if name in ("ceildiv", "cdiv") and len(args) == 2:
                 return Bin("//", Bin("+", args[0], Bin("-", args[1], Const(1))), args[1])
             if name == "clamp":  # min(max(value, low), high), as the reference reads it (frontend.py:1098-1102)
-                if len(args) != 3:
+                kwe = {k.arg: self.expr(k.value) for k in node.keywords}
+                names = ("dst", "min_val", "max_val")
+                vals = list(args) + [kwe[n] for n in names[len(args):] if n in kwe]
+                if len(vals) != 3:
                     self.fail(node, "T.clamp takes (value, min_val, max_val)")
-                return Call("min", (Call("max", (args[0], args[1])), args[2]))
+                return Call("min", (Call("max", (vals[0], vals[1])), vals[2]))
             if name in _MATH_FUNCS:
                 fn = _MATH_FUNCS[name]
                 if fn in ("//", "%", "&", "|", "^", "<<", ">>"):
@@ -777,6 +791,8 @@ class _Reader:
                 return stmts
             if len(tnames) != 1:
                 self.fail(node, "Serial loops bind a single variable")
+            if not args and "stop" in kw:
+                args = ([kw["start"]] if "start" in kw else []) + [kw["stop"]]
             if not args or len(args) > 3:
                 self.fail(node, "serial loops take (stop), (start, stop) or (start, stop, step)")
             start, stop = (Const(0), args[0]) if len(args) == 1 else (args[0], args[1])
