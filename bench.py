@@ -588,11 +588,32 @@ def run_op(op, torch, dist, world, steps, warmup, stream, peaks, peak_kind, traf
                      "traffic": tr.get("bytes_per_launch") if isinstance(tr, dict) else None,
                      "algorithmic_per_launch": units},
     }
+    result["python_call"] = measure_call_path(op, torch, stream)
     if want_e2e:
         result["e2e"] = measure_e2e(op, torch, dist, world, steps, stream)
     op.sets = None
     torch.cuda.empty_cache()
     return result
+
+
+def measure_call_path(op, torch, stream, calls=200):
+    """The drop-in call path: CompiledKernel.__call__ (argument checks, ctypes, launch) on
+    device-resident tensors, timed on the host over back-to-back calls.  When the host cost
+    per call exceeds the kernel time the GPU waits on Python, and us_per_call is the host cost."""
+    kern = op.kernel
+    nsets = len(op.sets)
+    n = calls if op.bound == "hbm" else max(5, min(calls, 20))
+    with torch.cuda.stream(stream):
+        for i in range(3):
+            kern(*op.sets[i % nsets][0])
+        stream.synchronize()
+        t0 = time.perf_counter()
+        for i in range(n):
+            kern(*op.sets[i % nsets][0])
+        t_issue = time.perf_counter() - t0
+        stream.synchronize()
+        t_all = time.perf_counter() - t0
+    return {"us_per_call": round(1e6 * t_all / n, 2), "host_us_per_call": round(1e6 * t_issue / n, 2), "calls": n}
 
 
 def measure_e2e(op, torch, dist, world, steps, stream):

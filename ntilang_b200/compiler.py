@@ -32,10 +32,19 @@ from .frontend import Program, read_program
 from .ir import DTYPES, CompileError, ScalarParameter, SymDim
 from .language import PrimFunc, SymbolicDim, SymbolicTensorSpec
 from .export import standalone_module
-from .launch import describe, launch
+from .launch import describe, make_launcher
 from .pointwise import lower as lower_pointwise
 from .pointwise import validate_scalar
 from .recognize import OpSpec, recognize
+
+
+def _current_stream(torch, index):
+    """torch's current CUDA stream on device ``index`` as a raw cudaStream_t (the stream TVM-FFI's
+    environment stream follows in the reference)."""
+    raw = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+    if raw is not None:
+        return raw(index)
+    return torch.cuda.current_stream(index).cuda_stream
 
 
 def _torch():
@@ -51,6 +60,8 @@ class CompiledKernel:
     out_idx: tuple = ()
     spec: OpSpec = None
     _built: bool = field(default=False, init=False, repr=False)
+    _state: object = field(default=None, init=False, repr=False)
+    _run: object = field(default=None, init=False, repr=False)
 
     has_gpu_module = True
 
@@ -136,6 +147,23 @@ class CompiledKernel:
             outs.append(torch.empty(shape, dtype=torch_dtype_for(param.type.dtype, torch), device=device))
         return outs
 
+    def _call_state(self):
+        """Per-kernel state of the call path, built on the first call: for each parameter its
+        static shape (None when symbolic), torch dtype and byte size."""
+        torch = _torch()
+        plan = []
+        for p in self.ir.params:
+            if isinstance(p, ScalarParameter):
+                plan.append(None)
+                continue
+            shape = tuple(p.type.shape)
+            static = not any(isinstance(d, SymDim) for d in shape)
+            size = DTYPES[p.type.dtype]
+            for d in shape if static else ():
+                size *= d
+            plan.append((p, shape if static else None, torch_dtype_for(p.type.dtype, torch), size if static else None))
+        return plan
+
     def __call__(self, *arguments):
         params = self.ir.params
         allocated = None
@@ -156,45 +184,70 @@ class CompiledKernel:
             missing = [s.name for s in self.ir.sym_dims if s.name not in bindings]
             if missing:
                 raise ValueError(f"Unbound symbolic dimensions: {', '.join(missing)}")
+        if self._state is None:
+            self._state = self._call_state()
+        plan = self._state
+        torch = _torch()
+        tensor_type = torch.Tensor
         devices = set()
         ranges = []
         checked = []
-        for tensor, param in zip(arguments, params):
-            if isinstance(param, ScalarParameter):
+        first = None
+        for tensor, param, entry in zip(arguments, params, plan):
+            if entry is None:
                 checked.append(validate_scalar(tensor, param))
                 continue
             checked.append(tensor)
-            if not hasattr(tensor, "__dlpack_device__") or tensor.__dlpack_device__()[0] != 2:
-                raise TypeError(f"{param.name} must be a CUDA tensor supporting DLPack")
-            devices.add(tensor.__dlpack_device__()[1])
-            expected = self._resolve(param.type.shape, bindings)
-            if tuple(tensor.shape) != expected:
-                raise ValueError(f"{param.name}: expected shape {expected}, got {tuple(tensor.shape)}")
-            if str(tensor.dtype).split(".")[-1] != param.type.dtype:
-                raise ValueError(f"{param.name}: expected dtype {param.type.dtype}, got {tensor.dtype}")
+            _, static_shape, tdtype, static_size = entry
+            if type(tensor) is tensor_type:  # fast path: a torch tensor
+                if not tensor.is_cuda:
+                    raise TypeError(f"{param.name} must be a CUDA tensor supporting DLPack")
+                devices.add(tensor.get_device())
+                expected = static_shape if static_shape is not None else self._resolve(param.type.shape, bindings)
+                if tensor.shape != expected:
+                    raise ValueError(f"{param.name}: expected shape {expected}, got {tuple(tensor.shape)}")
+                if tensor.dtype is not tdtype:
+                    raise ValueError(f"{param.name}: expected dtype {param.type.dtype}, got {tensor.dtype}")
+            else:
+                if not hasattr(tensor, "__dlpack_device__") or tensor.__dlpack_device__()[0] != 2:
+                    raise TypeError(f"{param.name} must be a CUDA tensor supporting DLPack")
+                devices.add(tensor.__dlpack_device__()[1])
+                expected = self._resolve(param.type.shape, bindings)
+                if tuple(tensor.shape) != expected:
+                    raise ValueError(f"{param.name}: expected shape {expected}, got {tuple(tensor.shape)}")
+                if str(tensor.dtype).split(".")[-1] != param.type.dtype:
+                    raise ValueError(f"{param.name}: expected dtype {param.type.dtype}, got {tensor.dtype}")
             if not tensor.is_contiguous():
                 raise ValueError(f"{param.name} must be contiguous in row-major order")
             pointer = tensor.data_ptr()
             if pointer % 16:
                 raise ValueError(f"{param.name} requires a tensor with an inspectable, 16-byte-aligned data pointer")
-            size = DTYPES[param.type.dtype]
-            for d in expected:
-                size *= d
+            size = static_size
+            if size is None:
+                size = DTYPES[param.type.dtype]
+                for d in expected:
+                    size *= d
             for start, end, name in ranges:
                 if pointer < end and start < pointer + size:
                     raise ValueError(f"Tensor arguments {name} and {param.name} must have disjoint storage")
             ranges.append((pointer, pointer + size, param.name))
+            if first is None:
+                first = tensor
         if len(devices) > 1:
             raise ValueError("All tensor arguments must be on the same CUDA device")
         if not devices:
             raise TypeError("a kernel launch needs at least one CUDA tensor argument")
         if not self._built:
             self.build()
-        torch = _torch()
-        device = next(a.device for a, p in zip(arguments, params) if not isinstance(p, ScalarParameter))
-        with torch.cuda.device(device):
-            stream = torch.cuda.current_stream(device).cuda_stream
-            launch(self.spec, checked, stream, bindings)
+        run = self._run
+        if run is None:
+            run = self._run = make_launcher(self.spec)
+        (index,) = devices
+        if index == torch.cuda.current_device():
+            run(checked, _current_stream(torch, index), bindings)
+        else:
+            with torch.cuda.device(first.device):
+                run(checked, _current_stream(torch, index), bindings)
         if allocated is not None:
             return allocated[0] if len(allocated) == 1 else tuple(allocated)
         return None

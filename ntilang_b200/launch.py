@@ -127,6 +127,44 @@ def launch(spec: OpSpec, tensors, stream: int, bindings=None) -> None:
         _lib.call(entry, *_recipe_args(recipe, tensors, stream))
 
 
+def _getter(item):
+    kind = item[0]
+    if kind == "ptr":
+        i = item[1]
+        return lambda t, s: t[i].data_ptr()
+    if kind == "null":
+        return lambda t, s: None
+    if kind in ("i32", "i64", "f32"):
+        v = item[1]
+        return lambda t, s: v
+    if kind == "dim":
+        i, d = item[1], item[2]
+        return lambda t, s: t[i].shape[d]
+    if kind == "rows":
+        i = item[1]
+        return lambda t, s: (t[i].numel() // t[i].shape[-1]) if t[i].dim() > 1 else 1
+    return lambda t, s: s
+
+
+def make_launcher(spec: OpSpec):
+    """launch(spec, ...) with the per-op work done once: the C entry points bound and each
+    argument recipe turned into getters.  Returns ``run(tensors, stream, bindings)``."""
+    if spec.family == "pointwise":
+        kernel = spec.params["kernel"]
+        return lambda tensors, stream, bindings: kernel.launch(tensors, bindings, stream)
+    handle = _lib.lib()
+    calls = [(entry, getattr(handle, entry), tuple(_getter(it) for it in recipe)) for entry, recipe in abi_calls(spec)]
+
+    def run(tensors, stream, bindings):
+        for entry, fn, getters in calls:
+            rc = fn(*[g(tensors, stream) for g in getters])
+            if rc:
+                msg = handle.ntl_last_error()
+                raise _lib.KernelError(entry, rc, msg.decode() if msg else "")
+
+    return run
+
+
 ABI_CALL = {
     "elementwise": "ntl_binary_f32(op, A, B, C, n, stream)",
     "cumsum": "ntl_cumsum_f32(X, Y, rows, cols, reverse, stream)",

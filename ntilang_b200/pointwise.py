@@ -156,6 +156,7 @@ class PointwiseKernel:
     grid_args: tuple  # indices of grid dims passed as int64 arguments
     points: int  # CUDA threads per block instance (largest parallel domain)
     _handle: int = field(default=0, repr=False)
+    _fast: object = field(default=None, repr=False)
 
     def build(self) -> int:
         """Compile with NVRTC (host only) and return the library's kernel handle."""
@@ -174,24 +175,43 @@ class PointwiseKernel:
         return extents, total
 
     def launch(self, arguments, bindings: dict, stream: int) -> None:
-        handle = self.build()
-        extents, total = self.launch_geometry(bindings)
-        if total == 0:
+        fast = self._fast
+        if fast is None:
+            fast = self._fast = self._prepare()
+        fn, kinds, static = fast
+        if static is not None:
+            tail, grid_x = static
+        else:
+            extents, total = self.launch_geometry(bindings)
+            if total == 0:
+                return
+            tail = [ctypes.c_int64(int(bindings[s])) for s in self.sym_names]
+            tail += [ctypes.c_int64(int(extents[i])) for i in self.grid_args]
+            tail.append(ctypes.c_int64(total))
+            per_cta = BLOCK_THREADS * POINTS_PER_THREAD
+            grid_x = (total + per_cta - 1) // per_cta
+        if grid_x == 0:
             return
-        keep = []
-        for param, arg in zip(self.program.params, arguments):
-            if isinstance(param, ScalarParameter):
-                keep.append(_CTYPES_SCALAR[param.dtype](arg))
-            else:
-                keep.append(ctypes.c_void_p(arg.data_ptr()))
-        keep.extend(ctypes.c_int64(int(bindings[s])) for s in self.sym_names)
-        keep.extend(ctypes.c_int64(int(extents[i])) for i in self.grid_args)
-        keep.append(ctypes.c_int64(total))
-        argv = (ctypes.c_void_p * len(keep))(*[ctypes.cast(ctypes.pointer(k), ctypes.c_void_p) for k in keep])
-        per_cta = BLOCK_THREADS * POINTS_PER_THREAD
-        grid_x = (total + per_cta - 1) // per_cta
-        _lib.call("ntl_rtc_launch", ctypes.c_uint64(handle), ctypes.c_uint64(grid_x), ctypes.c_uint32(BLOCK_THREADS),
-                  argv, ctypes.c_void_p(stream))
+        keep = [ctypes.c_void_p(a.data_ptr()) if k is None else k(a) for k, a in zip(kinds, arguments)]
+        keep += tail
+        argv = (ctypes.c_void_p * len(keep))(*[ctypes.addressof(k) for k in keep])
+        rc = fn(self._handle, grid_x, BLOCK_THREADS, argv, stream)
+        if rc:
+            msg = _lib.lib().ntl_last_error()
+            raise _lib.KernelError("ntl_rtc_launch", rc, msg.decode() if msg else "")
+
+    def _prepare(self):
+        """Per-kernel launch state: the bound C entry, argument converters, and for programs
+        without symbolic sizes the fixed trailing arguments and grid."""
+        self.build()
+        fn = _lib.lib().ntl_rtc_launch
+        kinds = [(_CTYPES_SCALAR[p.dtype] if isinstance(p, ScalarParameter) else None) for p in self.program.params]
+        static = None
+        if not self.sym_names and not self.grid_args:
+            _, total = self.launch_geometry({})
+            per_cta = BLOCK_THREADS * POINTS_PER_THREAD
+            static = ([ctypes.c_int64(total)], (total + per_cta - 1) // per_cta)
+        return fn, kinds, static
 
 
 def _eval_host(e, bindings):

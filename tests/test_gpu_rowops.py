@@ -78,6 +78,25 @@ def test_nondefault_stream(torch_cuda):
     torch.testing.assert_close(c, expected, rtol=0, atol=0)
 
 
+def test_launch_follows_the_current_stream(torch_cuda):
+    """The kernel runs on torch's current stream: ordered after work queued on that stream
+    (here a ~50 ms sleep, then the fills), never on the legacy stream."""
+    torch = torch_cuda
+    n = 1 << 20
+    kernel = K.vector_add(n)
+    a = torch.zeros(n, device="cuda")
+    b = torch.zeros_like(a)
+    torch.cuda.synchronize()
+    side = torch.cuda.Stream()
+    with torch.cuda.stream(side):
+        torch.cuda._sleep(100_000_000)
+        a.fill_(1.0)
+        b.fill_(2.0)
+        c = kernel(a, b)
+    side.synchronize()
+    assert bool(torch.all(c == 3.0))
+
+
 # ------------------------------------------------------------------------------- cumsum
 
 
