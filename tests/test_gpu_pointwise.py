@@ -196,3 +196,66 @@ def test_large_generic_fma_matches_oracle_sample(torch_cuda):
     kern(a, b, c, d)
     torch.cuda.synchronize()
     assert torch.equal(d, a * b + c)
+
+
+def _run_against_oracle(torch, kern, arrays, scalars=()):
+    """Run a generic kernel on the GPU and the oracle evaluator on copies; compare bitwise."""
+    gpu_args = [to_gpu(torch, a) for a in arrays]
+    kern(*gpu_args, *scalars)
+    torch.cuda.synchronize()
+    expect = [a.copy() for a in arrays]
+    pointwise_eval.evaluate(kern.ir, expect, scalars)
+    for got, want in zip(gpu_args, expect):
+        np.testing.assert_array_equal(got.cpu().numpy(), want)
+
+
+def test_three_d_grid_symbolic_rows_and_two_loop_shapes(torch_cuda):
+    """A 3-D grid whose first extent is symbolic, an integer scalar, and two T.Parallel loops
+    of different shapes in one kernel (each thread covers the larger domain)."""
+    torch = torch_cuda
+    R = T.dynamic("r")
+
+    @T.prim_func
+    def grid3(X: T.Tensor((R, 6, 40), "float32"), Y: T.Tensor((R, 6, 40), "float32"),
+              Z: T.Tensor((R, 6), "int32"), shift: T.int32):
+        with T.Kernel(T.ceildiv(40, 16), 6, R, threads=64) as (bx, by, bz):
+            for i in T.Parallel(16):
+                Y[bz, by, bx * 16 + i] = X[bz, by, bx * 16 + i] * 2.0 - T.cast(shift, "float32")
+            for j in T.Parallel(4):
+                if bx == 0 and j == 0:
+                    Z[bz, by] = bz * 100 + by * 10 + shift
+
+    kern = ntilang.compile(grid3)
+    assert kern.spec.family == "pointwise"
+    for rows in (1, 5):
+        rng = np.random.default_rng(rows)
+        arrays = [rng.normal(size=(rows, 6, 40)).astype(np.float32), np.full((rows, 6, 40), np.nan, np.float32),
+                  np.zeros((rows, 6), np.int32)]
+        _run_against_oracle(torch, kern, arrays, (7,))
+
+
+def test_region_copy_and_narrow_and_wide_dtypes(torch_cuda):
+    """A global-to-global T.copy of a tile region, int8/uint8 wrap-around arithmetic and float64."""
+    torch = torch_cuda
+
+    @T.prim_func
+    def mixed_types(A: T.Tensor((50, 70), "float32"), B: T.Tensor((50, 70), "float32"),
+                    C: T.Tensor((300,), "int8"), D: T.Tensor((300,), "uint8"), E: T.Tensor((300,), "float64"),
+                    F: T.Tensor((300,), "float64")):
+        with T.Kernel(T.ceildiv(70, 32), T.ceildiv(50, 16), threads=128) as (bx, by):
+            T.copy(A[by * 16:by * 16 + 16, bx * 32:bx * 32 + 32], B[by * 16:by * 16 + 16, bx * 32:bx * 32 + 32])
+            for k in T.Parallel(128):
+                idx = (by * 3 + bx) * 128 + k
+                c = C[idx]
+                C[idx] = c * c + T.cast(7, "int8")
+                d = D[idx]
+                D[idx] = d * T.cast(3, "uint8") + d
+                F[idx] = E[idx] * E[idx] / 3.0 + E[idx]
+
+    kern = ntilang.compile(mixed_types)
+    assert kern.spec.family == "pointwise"
+    rng = np.random.default_rng(11)
+    arrays = [rng.normal(size=(50, 70)).astype(np.float32), np.full((50, 70), np.nan, np.float32),
+              rng.integers(-128, 127, size=300).astype(np.int8), rng.integers(0, 255, size=300).astype(np.uint8),
+              rng.normal(size=300), np.full(300, np.nan)]
+    _run_against_oracle(torch, kern, arrays)
