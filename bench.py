@@ -1,7 +1,7 @@
 #!/usr/bin/env python
 """Throughput of the hot-path kernels on B200 (one process per GPU).
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--ops a,b,...]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference|reference-gpu] [--ops a,b,...]
 
 A *step* is one launch of an op over one batch of synthetic input with BASELINE.json's
 shapes and distributions.  The headline line is the configuration BASELINE.json's metric
@@ -303,6 +303,19 @@ class VaddOp(RowOp):
         return n * 3 * m * 4 / dt / 1e9, f"{n} x vector add [{m}]"
 
 
+def generic_fma_program(T, n, block=1024):
+    """D = A * B + C as a TileLang program, built with whichever package's ``T`` is passed."""
+
+    @T.prim_func
+    def generic_fma(A: T.Tensor((n,), "float32"), B: T.Tensor((n,), "float32"), C: T.Tensor((n,), "float32"),
+                    D: T.Tensor((n,), "float32")):
+        with T.Kernel(T.ceildiv(n, block), threads=256) as b:
+            for k in T.Parallel(block):
+                D[b * block + k] = A[b * block + k] * B[b * block + k] + C[b * block + k]
+
+    return generic_fma
+
+
 class GenericFmaOp(RowOp):
     """A program outside the recognised families: CUDA C generated per program, NVRTC-compiled."""
 
@@ -311,19 +324,10 @@ class GenericFmaOp(RowOp):
     config = "generic elementwise D = A*B + C (separately rounded), A,B,C f32 [16777216] ~N(0,1), NVRTC path"
 
     def setup(self):
-        import ntilang
-        import ntilang.language as T
+        import ntilang_b200
+        from ntilang_b200 import language as T
 
-        n, block = self.n, 1024
-
-        @T.prim_func
-        def generic_fma(A: T.Tensor((n,), "float32"), B: T.Tensor((n,), "float32"), C: T.Tensor((n,), "float32"),
-                        D: T.Tensor((n,), "float32")):
-            with T.Kernel(T.ceildiv(n, block), threads=256) as b:
-                for k in T.Parallel(block):
-                    D[b * block + k] = A[b * block + k] * B[b * block + k] + C[b * block + k]
-
-        self.kernel = ntilang.compile(generic_fma, out_idx=[-1])
+        self.kernel = ntilang_b200.compile(generic_fma_program(T, self.n), out_idx=[-1])
         assert self.kernel.spec.family == "pointwise"
         k = self.sets_needed(4 * self.n * 4)
         self.sets = []
@@ -669,6 +673,159 @@ def cpu_baseline(op, seconds):
     return {"value": round(value, 4), "unit": op.unit, "cores": cores, "kind": "port", "sample": sample}
 
 
+# ------------------------------------------------------------------------------ the reference's kernels on the GPU
+
+REF_INSTALL = ROOT / "baseline" / "_ref"
+
+
+def reference_builders(target):
+    """The reference's own kernels for each op at the bench shapes.
+
+    Each is built by the reference's unmodified examples/*.py through its own ``compile``
+    (CuTe DSL code generation, then cute.compile for ``target``) and launched through its own
+    ``CompiledKernel.__call__`` (TVM-FFI on torch's current stream).  The GEMMs use the tiles
+    of the reference's README benchmark (README.md:38-58: 128x128x32, 3 stages, swizzle panel
+    8); everything else uses the examples' defaults.  name -> (make(op) -> kernel,
+    args(our argument tuple, op) -> the reference's argument tuple, expected(args) -> the
+    output to compare against or None to compare with our kernel's output)."""
+    import importlib
+
+    import ntilang as R
+    import ntilang.language as RT
+
+    def ex(module, fn=None):
+        return getattr(importlib.import_module(f"examples.{module}"), fn or module)
+
+    same = lambda a, op: a  # noqa: E731
+
+    def relu_args(a, op):
+        x, w, bias, c = a
+        return x, w, bias.expand(op.m, op.n).contiguous(), c
+
+    gemm_tiles = dict(block_m=128, block_n=128, block_k=32, num_stages=3, swizzle_panel=8, target=target)
+    return {
+        "cumsum": (lambda op: ex("cumsum")(op.rows, op.cols, target=target), same, None),
+        "rmsnorm": (lambda op: ex("rmsnorm")(op.rows, op.cols, eps=op.eps, target=target), same, None),
+        "layernorm": (lambda op: ex("layernorm")(op.rows, op.cols, eps=op.eps, target=target), same, None),
+        "softmax": (lambda op: ex("softmax")(op.rows, op.cols, target=target), same, None),
+        "vadd": (lambda op: ex("vector_add")(op.n, target=target), same, None),
+        "transpose": (lambda op: ex("transpose")(op.m, op.n, target=target), same, None),
+        "gemm": (lambda op: ex("matmul")(op.m, op.n, op.k, **gemm_tiles), same, None),
+        # The example's epilogue is relu(0.5 * acc + Bias[M, N]) (examples/matmul_relu.py:35-38):
+        # bias[N] is broadcast to a full [M, N] operand and the result checked against torch.
+        "gemm_bias_relu": (lambda op: ex("matmul_relu")(op.m, op.n, op.k, **gemm_tiles), relu_args,
+                           lambda a: (0.5 * (a[0].float() @ a[1].float()) + a[2]).relu()),
+        "fa2": (lambda op: ex("flash_attention")(op.B, op.H, op.S, op.D, is_causal=False, target=target), same,
+                None),
+        "fa2_causal": (lambda op: ex("flash_attention")(op.B, op.H, op.S, op.D, is_causal=True, target=target),
+                       same, None),
+        "pointwise": (lambda op: R.compile(generic_fma_program(RT, op.n), target=target), same, None),
+    }
+
+
+# max |ref - expected| allowed per op (atol + rtol * |expected|): bit-exact where both follow one
+# operation order.  For the generic D = A*B + C the reference's compiled kernel may contract the
+# multiply-add into one FMA (its evaluator and ours round twice): up to a few fp32 ulps apart.
+REF_TOLERANCE = {"cumsum": (0.0, 0.0), "vadd": (0.0, 0.0), "transpose": (0.0, 0.0), "pointwise": (4.8e-7, 1e-6),
+                 "rmsnorm": (1e-5, 1e-6), "layernorm": (1e-5, 1e-6), "softmax": (1e-5, 1e-7),
+                 "gemm": (1e-3, 1e-5), "gemm_bias_relu": (1e-3, 1e-5), "fa2": (0.0, 2e-3), "fa2_causal": (0.0, 2e-3)}
+
+
+def run_reference_gpu(args, ops):
+    """The reference's own GPU kernels (CuTe DSL, sm_80-style mma.sync / cp.async code compiled
+    for sm_100a) timed on this GPU beside ours: same shapes, inputs and buffer rotation.
+
+    The reference launches through TVM-FFI and takes no stream argument, so everything here
+    runs on torch's default stream and every check synchronises the whole device.  Timing:
+    K eager launches through ``CompiledKernel.__call__`` between CUDA events, queued behind a
+    short ``torch.cuda._sleep`` so the host's call overhead does not show in the kernel time
+    (its host cost per call is reported separately).  Needs the reference package and its
+    examples under baseline/_ref."""
+    if not (REF_INSTALL / "ntilang" / "__init__.py").exists() or not (REF_INSTALL / "examples").is_dir():
+        print(json.dumps({"impl": "reference-gpu", "unavailable": f"no reference package under {REF_INSTALL}"}))
+        return 0
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    sys.path.insert(0, str(REF_INSTALL))
+    os.environ.setdefault("NTILANG_CACHE_DIR", str(Path("/tmp") / "ntilang_ref_cache"))
+    import ntilang
+    import torch
+
+    if not Path(ntilang.__file__).resolve().is_relative_to(REF_INSTALL.resolve()):
+        raise SystemExit(f"ntilang resolved to {ntilang.__file__}, not the reference under {REF_INSTALL}")
+    torch.cuda.set_device(0)
+    device = torch.device("cuda:0")
+    major, minor = torch.cuda.get_device_capability(device)
+    target = f"sm_{major}{minor}a" if major >= 9 else f"sm_{major}{minor}"
+    builders = reference_builders(target)
+    peaks, peak_kind = load_peaks()
+    stream = torch.cuda.current_stream(device)
+    sampler = ClockSampler(0)
+    sampler.start()
+    results = {}
+    steps = max(1, args.steps)
+    for name in ops:
+        op = OPS[name](torch, device, 0)
+        make, to_ref, expected = builders[name]
+        t0 = time.perf_counter()
+        try:
+            kern = make(op)
+            kern.build()
+        except Exception as exc:  # noqa: BLE001 - a kernel the reference cannot build is reported
+            results[name] = {"unavailable": f"reference build failed: {type(exc).__name__}: {str(exc)[:160]}"}
+            continue
+        build_s = time.perf_counter() - t0
+        op.setup()
+        sets = [to_ref(s[0], op) for s in op.sets]
+        kern(*sets[0])
+        torch.cuda.synchronize()
+        want = op.kernel(*op.sets[0][1]) if expected is None else expected(sets[0])
+        torch.cuda.synchronize()
+        got = sets[0][-1]
+        diff = (got.float() - want.float()).abs()
+        rtol, atol = REF_TOLERANCE[name]
+        bound = atol + rtol * want.float().abs()
+        check = {"max_abs_diff": float(diff.max().item()), "within": bool((diff <= bound).all().item()),
+                 "mismatches": int((diff > bound).sum().item()), "against": "ours" if expected is None else "torch",
+                 "rtol": rtol, "atol": atol}
+        del want, diff, bound
+        for i in range(max(3, args.warmup)):
+            kern(*sets[i % len(sets)])
+        torch.cuda.synchronize()
+        t1 = time.perf_counter()
+        for i in range(steps):
+            kern(*sets[i % len(sets)])
+        host_us = 1e6 * (time.perf_counter() - t1) / steps
+        torch.cuda.synchronize()
+        start = torch.cuda.Event(enable_timing=True)
+        end = torch.cuda.Event(enable_timing=True)
+        # a head start of ~2x the host time of K calls (at <= 2 GHz), so the launches queue up
+        torch.cuda._sleep(int(min(2e8, 2 * host_us * steps * 2000)))
+        start.record(stream)
+        for i in range(steps):
+            kern(*sets[i % len(sets)])
+        end.record(stream)
+        torch.cuda.synchronize()
+        ms_step = start.elapsed_time(end) / steps
+        units = op.units()
+        value = units / (ms_step / 1e3) / op.per_unit()
+        key = "hbm_gbs" if op.bound == "hbm" else "bf16_tflops"
+        peak = float(peaks.get(key, FALLBACK_PEAKS[key]))
+        results[name] = {"value": round(value, 3), "unit": op.unit, "ms_per_step": round(ms_step, 6),
+                         "frac_of_peak": round(value / peak, 4), "peak": peak, "peak_source": peak_kind,
+                         "config": op.config, "build_seconds": round(build_s, 2), "check": check,
+                         "host_us_per_call": round(host_us, 2), "buffer_sets": len(sets),
+                         "timing": "K eager launches through CompiledKernel.__call__ on the default stream, "
+                                   "queued behind torch.cuda._sleep, CUDA events"}
+        op.sets = sets = None
+        torch.cuda.empty_cache()
+    clocks = sampler.stop()
+    print(json.dumps({"impl": "reference-gpu", "target": target, "n_gpus": 1, "steps": steps,
+                      "warmup": args.warmup, "clocks": clocks, "ops": results}), flush=True)
+    return 0
+
+
 # ------------------------------------------------------------------------------ driver
 
 
@@ -677,7 +834,7 @@ def main():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
-    ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    ap.add_argument("--impl", choices=("ours", "reference", "reference-gpu"), default="ours")
     ap.add_argument("--ops", default=",".join(OPS))
     ap.add_argument("--cpu-seconds", type=float, default=2.0, help="CPU-baseline sample per op (0 = skip)")
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer end-to-end leg")
@@ -703,6 +860,8 @@ def main():
         ops.insert(0, HEADLINE)
     if args.impl == "reference":
         return run_reference(args, ops)
+    if args.impl == "reference-gpu":
+        return run_reference_gpu(args, ops)
     return run_ours(args, ops)
 
 
