@@ -71,6 +71,7 @@ struct __align__(16) Fa2Ctl {
   uint64_t sm_done[QTILES];
   uint64_t p_lo[QTILES];     // the low-key half of P_i is in TMEM (8 warps)
   uint64_t o_final[QTILES];
+  uint64_t o_staged[QTILES];  // O_i / l is in shared memory (4 warps)
   uint64_t drain;
   uint32_t tmem_base;
   int abort;
@@ -160,6 +161,7 @@ template <int D>
 __global__ void __launch_bounds__(THREADS, 1) fa2_fwd_kernel(const __grid_constant__ CUtensorMap tq,
                                                              const __grid_constant__ CUtensorMap tk,
                                                              const __grid_constant__ CUtensorMap tv,
+                                                             const __grid_constant__ CUtensorMap to,
                                                              const Fa2Params p) {
   using L = Fa2Smem<D>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -191,6 +193,7 @@ __global__ void __launch_bounds__(THREADS, 1) fa2_fwd_kernel(const __grid_consta
       mbar_init(&ctl->sm_done[i], SM_WARPS_PER_TILE);
       mbar_init(&ctl->p_lo[i], SM_WARPS_PER_TILE);
       mbar_init(&ctl->o_final[i], 1);
+      mbar_init(&ctl->o_staged[i], SM_WARPS_PER_TILE);
     }
     mbar_init(&ctl->drain, 1);
     ctl->abort = 0;
@@ -198,6 +201,7 @@ __global__ void __launch_bounds__(THREADS, 1) fa2_fwd_kernel(const __grid_consta
     prefetch_tensormap(&tq);
     prefetch_tensormap(&tk);
     prefetch_tensormap(&tv);
+    prefetch_tensormap(&to);
   }
   if (warp == MMA_WARP) {
     tmem_alloc(&ctl->tmem_base, TMEM_COLS);
@@ -458,7 +462,10 @@ __global__ void __launch_bounds__(THREADS, 1) fa2_fwd_kernel(const __grid_consta
       __syncwarp();
       if (lane == 0) mbar_arrive(&ctl->sm_done[i]);
     }
-    // epilogue: O / l -> fp16, the thread's row
+    // epilogue: O / l -> fp16.  Each thread writes its row into Q_i's shared buffer (free:
+    // Q_i's last QK^T retired before o_final) in the layout the 128-byte-swizzled Q tiles
+    // have, and one thread stores the tile with one TMA store per 64-column box; the tensor
+    // map clips rows past S.
     if (ok && n_mine > 0) {
       if (!mbar_wait_bounded(&ctl->o_final[i], 0, p.wait_limit, abort_flag)) {
         if (!*abort_flag) fa2_abort(ctl, NTL_STATUS_SOFTMAX_WAIT);
@@ -466,24 +473,37 @@ __global__ void __launch_bounds__(THREADS, 1) fa2_fwd_kernel(const __grid_consta
         __syncwarp();
         tc_fence_after();
         const float inv_l = 1.0f / l;
-        __half* orow = p.o + (static_cast<int64_t>(bh) * p.S + qrow) * D;
         uint32_t ov[D];  // the row of O: every chunk in flight before one wait
 #pragma unroll
         for (int ch = 0; ch < D / 32; ++ch)
           tmem_ld_32x32b_x32(o_addr + ch * 32, *reinterpret_cast<uint32_t(*)[32]>(ov + ch * 32));
         tc_wait_ld();
-        if (qrow < p.S) {
+        uint8_t* ot = smem + L::Q_OFF + i * L::Q_BYTES;
 #pragma unroll
-          for (int ch = 0; ch < D / 32; ++ch) {
-            uint32_t hv[16];
+        for (int ch = 0; ch < D / 32; ++ch) {
+          uint32_t hv[16];
 #pragma unroll
-            for (int e = 0; e < 16; ++e)
-              hv[e] = pack_half2(__uint_as_float(ov[ch * 32 + 2 * e]) * inv_l,
-                                 __uint_as_float(ov[ch * 32 + 2 * e + 1]) * inv_l);
-            uint4* dst = reinterpret_cast<uint4*>(orow + ch * 32);
+          for (int e = 0; e < 16; ++e)
+            hv[e] = pack_half2(__uint_as_float(ov[ch * 32 + 2 * e]) * inv_l,
+                               __uint_as_float(ov[ch * 32 + 2 * e + 1]) * inv_l);
 #pragma unroll
-            for (int q4 = 0; q4 < 4; ++q4)
-              dst[q4] = make_uint4(hv[4 * q4], hv[4 * q4 + 1], hv[4 * q4 + 2], hv[4 * q4 + 3]);
+          for (int q4 = 0; q4 < 4; ++q4) {
+            const int u = ch * 4 + q4;  // 16-byte unit of the row; 8 units per 64-column box
+            uint8_t* dst = ot + (u >> 3) * (BM * 128) + r * 128 + (((u & 7) ^ (r & 7)) << 4);
+            *reinterpret_cast<uint4*>(dst) = make_uint4(hv[4 * q4], hv[4 * q4 + 1], hv[4 * q4 + 2], hv[4 * q4 + 3]);
+          }
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&ctl->o_staged[i]);
+        if (quarter == 0 && lane == 0) {
+          if (mbar_wait_bounded(&ctl->o_staged[i], 0, p.wait_limit, abort_flag)) {
+#pragma unroll
+            for (int d = 0; d < D / 64; ++d) tma_store_3d(&to, ot + d * (BM * 128), d * 64, tile_q0, bh);
+            bulk_commit();
+            bulk_wait_read();
+          } else if (!*abort_flag) {
+            fa2_abort(ctl, NTL_STATUS_SOFTMAX_WAIT);
           }
         }
       }
@@ -531,8 +551,8 @@ int make_map_bshd(CUtensorMap* map, const void* base, uint64_t bh, uint64_t s, u
 }
 
 template <int D>
-int launch_fa2(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv, const Fa2Params& p,
-               cudaStream_t s) {
+int launch_fa2(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv, const CUtensorMap& mo,
+               const Fa2Params& p, cudaStream_t s) {
   static std::atomic<uint64_t> done_mask{0};
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return ntl_fail(NTL_ERR_CUDA, "cudaGetDevice failed");
@@ -553,7 +573,7 @@ int launch_fa2(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& 
                       fa.numRegs, REGS_LAUNCH);
   }
   const unsigned grid = static_cast<unsigned>(p.n_qb) * static_cast<unsigned>(p.BH);
-  fa2_fwd_kernel<D><<<grid, THREADS, Fa2Smem<D>::BYTES, s>>>(mq, mk, mv, p);
+  fa2_fwd_kernel<D><<<grid, THREADS, Fa2Smem<D>::BYTES, s>>>(mq, mk, mv, mo, p);
   ntl_note_launch();
   return ntl_check_launch("attention launch");
 }
@@ -583,11 +603,12 @@ extern "C" int ntl_fa2_fwd_f16(const uint16_t* q, const uint16_t* k, const uint1
   NTL_REQUIRE(seq < (int64_t(1) << 31), NTL_ERR_UNSUPPORTED, "attention: sequence too long");
   NTL_REQUIRE(((seq + BQ - 1) / BQ) * batch * heads < (int64_t(1) << 31), NTL_ERR_UNSUPPORTED,
               "attention: more than 2^31 - 1 (batch, head, 256-query block) blocks");
-  CUtensorMap mq, mk, mv;
+  CUtensorMap mq, mk, mv, mo;
   const uint64_t bh = static_cast<uint64_t>(batch * heads);
   if (int rc = make_map_bshd(&mq, q, bh, seq, dim)) return rc;
   if (int rc = make_map_bshd(&mk, k, bh, seq, dim)) return rc;
   if (int rc = make_map_bshd(&mv, v, bh, seq, dim)) return rc;
+  if (int rc = make_map_bshd(&mo, o, bh, seq, dim)) return rc;
   Fa2Params p;
   p.o = reinterpret_cast<__half*>(o);
   p.S = static_cast<int>(seq);
@@ -597,6 +618,6 @@ extern "C" int ntl_fa2_fwd_f16(const uint16_t* q, const uint16_t* k, const uint1
   p.c = scale_log2;
   p.wait_limit = ntl_wait_limit();
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  if (dim == 64) return launch_fa2<64>(mq, mk, mv, p, s);
-  return launch_fa2<128>(mq, mk, mv, p, s);
+  if (dim == 64) return launch_fa2<64>(mq, mk, mv, mo, p, s);
+  return launch_fa2<128>(mq, mk, mv, mo, p, s);
 }
