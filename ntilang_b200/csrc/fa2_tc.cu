@@ -60,12 +60,13 @@ struct Fa2Params {
   int S, n_qb;
   int BH;  // batch * heads
   int causal;
-  float c;  // softmax scale in log2 units
+  float c;          // softmax scale in log2 units
+  int succ_stride;  // CTAs resident at once: block b + succ_stride is likely to start when b ends
   int64_t wait_limit;
 };
 
 struct __align__(16) Fa2Ctl {
-  uint64_t q_full;
+  uint64_t q_full[QTILES];
   uint64_t k_full[KSTAGES], k_empty[KSTAGES], v_full[VSTAGES], v_empty[VSTAGES];
   uint64_t s_full[QTILES];
   uint64_t sm_done[QTILES];
@@ -178,8 +179,14 @@ __global__ void __launch_bounds__(THREADS, 1) fa2_fwd_kernel(const __grid_consta
   for (int i = 0; i < QTILES; ++i) n_t[i] = kv_tiles(p, q0 + i * BM);
   const int n_max = max(n_t[0], n_t[1]);
 
-  if (threadIdx.x == 0) {
-    mbar_init(&ctl->q_full, 1);
+  if (warp == TMA_WARP && lane == 0) {
+    // The load pipeline's barriers are set up by the thread that issues the loads, which
+    // starts Q_0, K_0 and Q_1 before the CTA-wide sync (a fresh K stage needs no empty
+    // wait), so the first QK^T's operands arrive during setup.  Then it prefetches into
+    // L2 the Q tiles of block b + succ_stride, which the hardware hands out in index order
+    // as CTAs retire: Q is read once per block, and without it the next block's first
+    // load on some SM would come from DRAM.
+    for (int i = 0; i < QTILES; ++i) mbar_init(&ctl->q_full[i], 1);
     for (int s = 0; s < KSTAGES; ++s) {
       mbar_init(&ctl->k_full[s], 1);
       mbar_init(&ctl->k_empty[s], 1);
@@ -188,6 +195,33 @@ __global__ void __launch_bounds__(THREADS, 1) fa2_fwd_kernel(const __grid_consta
       mbar_init(&ctl->v_full[s], 1);
       mbar_init(&ctl->v_empty[s], 1);
     }
+    fence_mbar_init();
+    prefetch_tensormap(&tq);
+    prefetch_tensormap(&tk);
+    auto load_q = [&](int i) {
+      mbar_arrive_expect_tx(&ctl->q_full[i], L::Q_BYTES);
+#pragma unroll
+      for (int d = 0; d < D / 64; ++d)
+        tma_load_3d(smem + L::Q_OFF + i * L::Q_BYTES + d * (BM * 128), &tq, &ctl->q_full[i], d * 64, q0 + i * BM, bh);
+    };
+    load_q(0);
+    mbar_arrive_expect_tx(&ctl->k_full[0], L::KV_BYTES);  // n_t[0] >= 1: q0 < S
+#pragma unroll
+    for (int d = 0; d < D / 64; ++d)
+      tma_load_3d(smem + L::K_OFF + d * (BN * 128), &tk, &ctl->k_full[0], d * 64, 0, bh);
+    load_q(1);
+    const int64_t succ = static_cast<int64_t>(blockIdx.x) + p.succ_stride;
+    if (p.succ_stride > 0 && succ < static_cast<int64_t>(gridDim.x)) {
+      int qb2, bh2;
+      decode_block(p, static_cast<int>(succ), qb2, bh2);
+#pragma unroll
+      for (int i = 0; i < QTILES; ++i)
+        if (qb2 * BQ + i * BM < p.S)
+#pragma unroll
+          for (int d = 0; d < D / 64; ++d) tma_prefetch_3d(&tq, d * 64, qb2 * BQ + i * BM, bh2);
+    }
+  }
+  if (threadIdx.x == 0) {
     for (int i = 0; i < QTILES; ++i) {
       mbar_init(&ctl->s_full[i], 1);
       mbar_init(&ctl->sm_done[i], SM_WARPS_PER_TILE);
@@ -198,8 +232,6 @@ __global__ void __launch_bounds__(THREADS, 1) fa2_fwd_kernel(const __grid_consta
     mbar_init(&ctl->drain, 1);
     ctl->abort = 0;
     fence_mbar_init();
-    prefetch_tensormap(&tq);
-    prefetch_tensormap(&tk);
     prefetch_tensormap(&tv);
     prefetch_tensormap(&to);
   }
@@ -216,16 +248,11 @@ __global__ void __launch_bounds__(THREADS, 1) fa2_fwd_kernel(const __grid_consta
   asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;\n" ::"n"(REGS_OTHER) : "memory");
   if (warp == TMA_WARP) {
     // ------------------------------------------------------------------ TMA producer
-    if (elect_one_lane()) {
+    if (lane == 0) {
       bool ok = true;
-      mbar_arrive_expect_tx(&ctl->q_full, QTILES * L::Q_BYTES);
-#pragma unroll
-      for (int i = 0; i < QTILES; ++i)
-#pragma unroll
-        for (int d = 0; d < D / 64; ++d)
-          tma_load_3d(smem + L::Q_OFF + i * L::Q_BYTES + d * (BM * 128), &tq, &ctl->q_full, d * 64, q0 + i * BM, bh);
-      // Issue order K0, K1, V0, K2, V1, ...: K runs one tile ahead of V.
-      int k_issued = 0, v_issued = 0;
+      // Q_0, K_0, Q_1 went out before the sync.  Issue order K0, K1, V0, K2, V1, ...: K runs
+      // one tile ahead of V.
+      int k_issued = 1, v_issued = 0;
       auto load_k = [&](int j) -> bool {
         const int s = j % KSTAGES;
         if (!mbar_wait_bounded(&ctl->k_empty[s], ((j / KSTAGES) & 1) ^ 1, p.wait_limit, abort_flag)) return false;
@@ -246,7 +273,6 @@ __global__ void __launch_bounds__(THREADS, 1) fa2_fwd_kernel(const __grid_consta
         ++v_issued;
         return true;
       };
-      if (n_max > 0) ok = load_k(0);
       for (int j = 0; j < n_max && ok; ++j) {
         if (j + 1 < n_max && !load_k(j + 1)) ok = false;
         else if (!load_v(j)) ok = false;
@@ -254,8 +280,9 @@ __global__ void __launch_bounds__(THREADS, 1) fa2_fwd_kernel(const __grid_consta
       if (!ok && !*abort_flag) fa2_abort(ctl, NTL_STATUS_TMA_EMPTY_WAIT);
       if (!ok) {
         // Drain every copy this thread issued before the CTA exits.
-        if (!mbar_wait_bounded(&ctl->q_full, 0, int64_t(1) << 24, nullptr))
-          atomicCAS(&g_fa2_status, 0u, NTL_STATUS_DRAIN_WAIT);
+        for (int i = 0; i < QTILES; ++i)
+          if (!mbar_wait_bounded(&ctl->q_full[i], 0, int64_t(1) << 24, nullptr))
+            atomicCAS(&g_fa2_status, 0u, NTL_STATUS_DRAIN_WAIT);
         for (int j = max(0, k_issued - KSTAGES); j < k_issued; ++j)
           if (!mbar_wait_bounded(&ctl->k_full[j % KSTAGES], (j / KSTAGES) & 1, int64_t(1) << 24, nullptr))
             atomicCAS(&g_fa2_status, 0u, NTL_STATUS_DRAIN_WAIT);
@@ -269,8 +296,7 @@ __global__ void __launch_bounds__(THREADS, 1) fa2_fwd_kernel(const __grid_consta
     if (elect_one_lane()) {
       constexpr uint32_t idesc_s = umma_idesc_f16_f32(BM, BN, 0, 0);  // B = K tile, K-major
       constexpr uint32_t idesc_o = umma_idesc_f16_f32(BM, D, 0, 1);   // B = V tile, N-major
-      bool ok = mbar_wait_bounded(&ctl->q_full, 0, p.wait_limit, abort_flag);
-      if (!ok && !*abort_flag) fa2_abort(ctl, NTL_STATUS_MMA_FULL_WAIT);
+      bool ok = true;
       auto spin_or_abort = [&](uint64_t* bar, uint32_t parity) -> bool {
         if (mbar_spin_bounded(bar, parity, p.wait_limit, abort_flag)) return true;
         if (!*abort_flag) fa2_abort(ctl, NTL_STATUS_MMA_FULL_WAIT);
@@ -292,11 +318,17 @@ __global__ void __launch_bounds__(THREADS, 1) fa2_fwd_kernel(const __grid_consta
         }
         tc_commit(&ctl->s_full[i]);
       };
-      if (ok && wait_or_abort(&ctl->k_full[0], 0)) {
-        tc_fence_after();
-        for (int i = 0; i < QTILES; ++i)
-          if (n_t[i] > 0) issue_s(i, 0);
-        tc_commit(&ctl->k_empty[0]);  // K_0 is free once both QK^T retire
+      if (wait_or_abort(&ctl->k_full[0], 0)) {
+        for (int i = 0; i < QTILES && ok; ++i) {
+          if (n_t[i] == 0) continue;
+          if (!wait_or_abort(&ctl->q_full[i], 0)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          issue_s(i, 0);
+        }
+        if (ok) tc_commit(&ctl->k_empty[0]);  // K_0 is free once both QK^T retire
       } else {
         ok = false;
       }
@@ -616,6 +648,9 @@ extern "C" int ntl_fa2_fwd_f16(const uint16_t* q, const uint16_t* k, const uint1
   p.BH = static_cast<int>(batch * heads);
   p.causal = causal ? 1 : 0;
   p.c = scale_log2;
+  int sms = 0;
+  if (int rc = ntl_num_sms(&sms)) return rc;
+  p.succ_stride = sms;  // one CTA per SM
   p.wait_limit = ntl_wait_limit();
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (dim == 64) return launch_fa2<64>(mq, mk, mv, mo, p, s);
