@@ -59,6 +59,10 @@ CTYPE = {
 }
 # C type of an element in memory.
 STORAGE = dict(CTYPE, float16="unsigned short", bfloat16="unsigned short")
+# Vector type of four elements of a storage type, for the 4-point groups of a vectorised
+# kernel (one 16-, 8- or 4-byte access instead of four scalar ones).
+VEC4 = {"float": "float4", "int": "int4", "unsigned": "uint4", "unsigned short": "ushort4", "short": "short4",
+        "signed char": "char4", "unsigned char": "uchar4"}
 # Unsigned type of the same width, for wrapping + - *.
 UNSIGNED = {"int8": "unsigned char", "int16": "unsigned short", "int32": "unsigned", "int64": "unsigned long long",
             "uint8": "unsigned", "uint16": "unsigned", "uint32": "unsigned", "uint64": "unsigned long long"}
@@ -233,9 +237,52 @@ def _eval_host(e, bindings):
     raise CompileError("grid extents must be integer expressions of symbolic sizes")
 
 
+def _buffer_uses(prog: Program):
+    """(loaded, stored) global buffer names of a program: read by a load, copy source or
+    atomic; written by a store, copy destination or atomic."""
+    loaded, stored = set(), set()
+
+    def walk(x):
+        if isinstance(x, (list, tuple)):
+            for y in x:
+                walk(y)
+            return
+        if not hasattr(x, "__dataclass_fields__"):
+            return
+        if isinstance(x, Load):
+            loaded.add(x.buf)
+        elif isinstance(x, Store):
+            stored.add(x.buf)
+        elif isinstance(x, Atomic):
+            loaded.add(x.buf)
+            stored.add(x.buf)
+        elif isinstance(x, Copy):
+            loaded.add(x.src.buf)
+            stored.add(x.dst.buf)
+        for f in x.__dataclass_fields__:
+            walk(getattr(x, f))
+
+    walk(prog.body)
+    return loaded, stored
+
+
 class _Lowering:
-    def __init__(self, prog: Program):
+    def __init__(self, prog: Program, vec: bool = False):
         self.prog = prog
+        # Vectorised form: thread t of a CTA takes the 4 consecutive points 4t .. 4t+3 of its
+        # 1024, and a global access whose 4 points are contiguous (unit stride in the innermost
+        # T.Parallel variable, index otherwise free of per-point values) becomes one vector
+        # access when the group is in bounds and aligned (checked at run time, else per point).
+        # Loads only from tensors the program never writes; stores only at the top level of a
+        # T.Parallel body to tensors it never reads (they are issued after the 4 points ran).
+        self.vec = vec
+        self.vec_decls: list = []  # declared before the point loop
+        self.vec_flush: list = []  # vector stores after the point loop
+        self.vec_loads: dict = {}  # (buffer, index) -> slot of a vectorised load
+        self.vec_count = 0
+        self.guard_sizes: list = []  # every `pt < n` guard
+        self.top_stmt = None  # the statement being lowered at the top level of a T.Parallel body
+        self.loaded, self.stored = _buffer_uses(prog)
         self.lines: list = []
         self.depth = 1
         self.types: dict = {}  # kernel variable -> dtype
@@ -316,6 +363,110 @@ class _Lowering:
             prods = [x * y for x in a for y in b]
             return (min(prods), max(prods))
         return None
+
+    # ---------------------------------------------------------- vector groups
+    def _vec_deps(self, e):
+        """Names an index expression depends on, or None when it holds anything but integer
+        constants, kernel values and + - * // %."""
+        if isinstance(e, Const):
+            return set() if isinstance(e.value, int) and not isinstance(e.value, bool) else None
+        if isinstance(e, Var):
+            return {e.name}
+        if isinstance(e, Bin) and e.op in ("+", "-", "*", "//", "%"):
+            a, b = self._vec_deps(e.a), self._vec_deps(e.b)
+            return None if a is None or b is None else a | b
+        return None
+
+    def _vec_group_ok(self, name, idx) -> bool:
+        """The 4 points of a group access 4 contiguous elements of ``name``."""
+        par = self.current_parallel
+        b = self.buf(name)
+        if not self.vec or par is None or b.scope != "global" or STORAGE[b.dtype] not in VEC4 or not idx:
+            return False
+        if par.extents[-1] % 4 or any(g % 4 for g in self.guards):
+            return False
+        inner = par.vars[-1]
+        free = set(self.prog.block_vars) | set(par.vars) | {f"$sym:{n}" for n in self.sym_names}
+        free |= {p.name for p in self.prog.params if isinstance(p, ScalarParameter)}
+        for e in idx[:-1]:
+            d = self._vec_deps(e)
+            if d is None or not d <= free or inner in d:
+                return False
+        if self.dtype(idx[-1]) not in ("int32", "int64", "uint32", "uint64"):
+            return False
+        return self._unit_stride(idx[-1], inner, free)
+
+    def _unit_stride(self, e, inner, free) -> bool:
+        """``e`` is ``inner`` plus / minus terms free of it, through + and - only.  Wrapping
+        integer + and - are linear modulo 2^32 (2^64), so the index of point u of a group is
+        the group's first index + u exactly whenever that sum stays below the type's maximum,
+        which the run-time group check asserts."""
+        if isinstance(e, Var) and e.name == inner:
+            return True
+        if not (isinstance(e, Bin) and e.op in ("+", "-")):
+            return False
+        da, db = self._vec_deps(e.a), self._vec_deps(e.b)
+        if da is None or db is None:
+            return False
+        if inner in da and inner not in db and db <= free:
+            return self._unit_stride(e.a, inner, free)
+        if e.op == "+" and inner in db and inner not in da and da <= free:
+            return self._unit_stride(e.b, inner, free)
+        return False
+
+    def _vec_group_check(self, name, idx, codes, off) -> str:
+        """Run-time test that a group's 4 elements are in bounds and vector-aligned."""
+        b = self.buf(name)
+        clauses = []
+        last = len(idx) - 1
+        for n, (e, c, d) in enumerate(zip(idx, codes, b.shape)):
+            if not isinstance(d, SymDim):
+                iv = self.interval(e)
+                if iv is not None and 0 <= iv[0] and iv[1] < d and iv[1] < 2**31 - 4:
+                    continue  # every point's index is in range (and far from wrapping), so the group's is
+            if n == last:  # the 4 indices c .. c+3 are in range and did not wrap
+                clauses.append(f"(0 <= ({c}) && (long long)({c}) + 3LL < {self.dim_code(d)} && "
+                               f"(long long)({c}) <= 2147483643LL)")
+            else:
+                clauses.append(f"(0 <= ({c}) && ({c}) < {self.dim_code(d)})")
+        size = 4 * DTYPES[b.dtype]
+        clauses.append(f"(((unsigned long long)(p_{_ident(name)} + ({off}))) & {size - 1}ULL) == 0ULL")
+        return " && ".join(clauses)
+
+    def vec_load(self, e: Load, codes):
+        if not self._vec_group_ok(e.buf, e.idx):
+            return None
+        key = (e.buf, repr(e.idx))
+        if key in self.vec_loads:
+            return self.vec_loads[key]
+        k = self.vec_count
+        self.vec_count += 1
+        self.vec_loads[key] = k
+        st = STORAGE[self.buf(e.buf).dtype]
+        vt = VEC4[st]
+        off = self.offset(e.buf, codes)
+        self.vec_decls += [f"bool vl{k}_ok = false;", f"{st} vl{k}_v[4];"]
+        self.emit("if (unit == 0) {")
+        self.emit(f"  const long long o_ = {off};")
+        self.emit(f"  vl{k}_ok = {self._vec_group_check(e.buf, e.idx, codes, 'o_')};")
+        self.emit(f"  if (vl{k}_ok) {{ const {vt} t_ = *reinterpret_cast<const {vt}*>(p_{_ident(e.buf)} + o_); "
+                  f"vl{k}_v[0] = t_.x; vl{k}_v[1] = t_.y; vl{k}_v[2] = t_.z; vl{k}_v[3] = t_.w; }}")
+        self.emit("}")
+        return k
+
+    def vec_store(self, name, idx, codes):
+        if not self._vec_group_ok(name, idx):
+            return None
+        k = self.vec_count
+        self.vec_count += 1
+        st = STORAGE[self.buf(name).dtype]
+        vt = VEC4[st]
+        off = self.offset(name, codes)
+        self.vec_decls += [f"bool vs{k}_ok = false;", f"long long vs{k}_o = 0;", f"{st} vs{k}_v[4];"]
+        self.emit(f"if (unit == 0) {{ vs{k}_o = {off}; vs{k}_ok = {self._vec_group_check(name, idx, codes, f'vs{k}_o')}; }}")
+        self.vec_flush.append(f"if (vs{k}_ok) *reinterpret_cast<{vt}*>(p_{_ident(name)} + vs{k}_o) = "
+                              f"make_{vt}(vs{k}_v[0], vs{k}_v[1], vs{k}_v[2], vs{k}_v[3]);")
+        return k
 
     def in_bounds(self, name, idx_exprs, idx_codes) -> str:
         shape = self.buf(name).shape
@@ -527,12 +678,17 @@ class _Lowering:
                     self.fail(f"{e.buf}: indices must be integers")
             pred = self.in_bounds(e.buf, e.idx, codes)
             elem = f"p_{_ident(e.buf)}[{self.offset(e.buf, codes)}]"
+            slot = self.vec_load(e, codes) if e.buf not in self.stored else None
+            if slot is not None:
+                elem = f"(vl{slot}_ok ? vl{slot}_v[unit] : {elem})"
             if b.dtype == "float16":
                 elem = f"ntl_h2f({elem})"
             elif b.dtype == "bfloat16":
                 elem = f"ntl_b2f({elem})"
             if pred:
                 zero = self.conv("0", "int32", b.dtype)
+                if slot is not None:
+                    return f"(vl{slot}_ok || ({pred}) ? {elem} : {zero})", b.dtype
                 return f"(({pred}) ? {elem} : {zero})", b.dtype
             return elem, b.dtype
         if b.scope == "var":
@@ -646,7 +802,7 @@ class _Lowering:
             self.emit(f"v_{_ident(s.name)} = {self.conv(code, d, self.types[s.name])};")
             return
         if isinstance(s, Store):
-            self.store(s.buf, s.idx, s.value)
+            self.store(s.buf, s.idx, s.value, top=s is self.top_stmt)
             return
         if isinstance(s, Atomic):
             self.atomic(s)
@@ -683,6 +839,7 @@ class _Lowering:
             low = self.low
             low.points = max(low.points, self.n)
             low.guards.append(self.n)
+            low.guard_sizes.append(self.n)
             low.emit(f"if (pt < {self.n}LL) {{")
             low.depth += 1
 
@@ -726,13 +883,16 @@ class _Lowering:
             self.current_parallel = s
             self.parallel_level += 1
             self.loops.append("parallel")
-            self.stmts(s.body)
+            for t in s.body:
+                self.top_stmt = t
+                self.stmt(t)
+            self.top_stmt = None
             self.loops.pop()
             self.parallel_level -= 1
             self.current_parallel = None
         self.ranges = saved
 
-    def store(self, name, idx, value):
+    def store(self, name, idx, value, top=False):
         b = self.buf(name)
         code, d = self.expr(value)
         if b.scope == "var":
@@ -753,6 +913,11 @@ class _Lowering:
         guard = pred
         if self.current_parallel is None and not self.guards:
             guard = f"pt == 0" + (f" && {pred}" if pred else "")  # one writer per block instance
+        slot = self.vec_store(name, idx, codes) if top and name not in self.loaded else None
+        if slot is not None:
+            self.emit(f"if (vs{slot}_ok) vs{slot}_v[unit] = {val};")
+            self.emit(f"else if ({guard}) {line}" if guard else f"else {line}")
+            return
         self.emit(f"if ({guard}) {line}" if guard else line)
 
     def atomic(self, s: Atomic):
@@ -868,11 +1033,21 @@ def _ident(name: str) -> str:
     return re.sub(r"[^0-9A-Za-z_]", "_", name)
 
 
-def lower(prog: Program) -> PointwiseKernel:
-    """Lower ``prog`` to CUDA C or raise ``CompileError`` when it is not elementwise."""
-    low = _Lowering(prog)
+def _lower_body(prog: Program, vec: bool) -> _Lowering:
+    low = _Lowering(prog, vec=vec)
     low.depth = 2
     low.stmts(prog.body)
+    return low
+
+
+def lower(prog: Program) -> PointwiseKernel:
+    """Lower ``prog`` to CUDA C or raise ``CompileError`` when it is not elementwise."""
+    low = _lower_body(prog, vec=False)
+    if low.points % 4 == 0 and all(n % 4 == 0 for n in low.guard_sizes):
+        vlow = _lower_body(prog, vec=True)
+        if vlow.vec_count:
+            low = vlow
+    vec = low.vec
     body = low.lines
     name = f"ntl_pw_{_ident(prog.name)}"
     params = []
@@ -906,10 +1081,17 @@ def lower(prog: Program) -> PointwiseKernel:
         "",
         f'extern "C" __global__ void __launch_bounds__({BLOCK_THREADS}) {name}(',
         "    " + ",\n    ".join(params) + ") {",
-        f"  const long long gbase = (long long)blockIdx.x * {BLOCK_THREADS * POINTS_PER_THREAD} + threadIdx.x;",
+    ]
+    if vec:  # thread t: points 4t .. 4t+3 of the CTA's run (a group never straddles a block instance)
+        head += [f"  const long long gbase = (long long)blockIdx.x * {BLOCK_THREADS * POINTS_PER_THREAD} + "
+                 f"(long long)threadIdx.x * {POINTS_PER_THREAD};"]
+        head += [f"  {d}" for d in low.vec_decls]
+    else:  # thread t: points t, t + 256, t + 512, t + 768 (each run coalesced)
+        head += [f"  const long long gbase = (long long)blockIdx.x * {BLOCK_THREADS * POINTS_PER_THREAD} + threadIdx.x;"]
+    head += [
         "#pragma unroll",
         f"  for (int unit = 0; unit < {POINTS_PER_THREAD}; ++unit) {{",
-        f"  const long long gid = gbase + (long long)unit * {BLOCK_THREADS};",
+        f"  const long long gid = gbase + (long long)unit * {1 if vec else BLOCK_THREADS};",
         "  if (gid >= total) break;",
         f"  const long long pt = gid % {points}LL;",
         f"  long long blk = gid / {points}LL;",
@@ -922,7 +1104,8 @@ def lower(prog: Program) -> PointwiseKernel:
             head.append(f"  blk /= {ext};")
     head.append("  (void)pt; (void)blk;")
     head.append("  {")
-    source = "\n".join(head + body + ["  }", "  }", "}", ""])
+    tail = ["  }", "  }"] + [f"  {f}" for f in low.vec_flush] + ["}", ""]
+    source = "\n".join(head + body + tail)
     return PointwiseKernel(name=name, source=source, program=prog, sym_names=low.sym_names, grid=tuple(prog.grid),
                            grid_args=tuple(low.grid_args), points=points)
 

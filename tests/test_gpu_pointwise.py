@@ -259,3 +259,36 @@ def test_region_copy_and_narrow_and_wide_dtypes(torch_cuda):
               rng.integers(-128, 127, size=300).astype(np.int8), rng.integers(0, 255, size=300).astype(np.uint8),
               rng.normal(size=300), np.full(300, np.nan)]
     _run_against_oracle(torch, kern, arrays)
+
+
+def test_vector_groups_and_their_per_point_fallbacks(torch_cuda):
+    """Unit-stride accesses of a T.Parallel point run as 4-point vector groups (16-byte fp32,
+    8-byte fp16, 4-byte int8 accesses); a group that is misaligned, crosses the tensor's end or
+    starts at a negative index falls back to per-point accesses, and a store inside a branch
+    stays per point.  Bit-exact against the oracle."""
+    torch = torch_cuda
+    n = 1003
+
+    @T.prim_func
+    def groups(A: T.Tensor((n,), "float32"), B: T.Tensor((n,), "float32"), C: T.Tensor((n,), "float32"),
+               H: T.Tensor((n,), "float16"), G: T.Tensor((n,), "float16"), I: T.Tensor((n,), "int8"),
+               J: T.Tensor((n,), "int8"), lo: T.int32):
+        with T.Kernel(T.ceildiv(n, 128), threads=128) as b:
+            for k in T.Parallel(128):
+                B[b * 128 + k] = A[k + (b * 128 + 1)] + A[k + (b * 128 + 4)]
+                if k >= lo:
+                    C[b * 128 + k] = A[k + b * 128] * 2.0
+                G[b * 128 + k] = H[b * 128 + k] * T.float16(1.5) + H[k + (b * 128 + 2)]
+                J[b * 128 + k] = I[b * 128 + k] * T.cast(3, "int8") + I[k + (b * 128 - 1)]
+
+    kern = ntilang.compile(groups)
+    assert kern.spec.family == "pointwise"
+    src = kern.get_cuda_source()
+    for vt in ("float4", "ushort4", "char4"):  # vector loads and stores for each element size
+        assert f"reinterpret_cast<const {vt}*>" in src and f"reinterpret_cast<{vt}*>" in src, vt
+    rng = np.random.default_rng(5)
+    for lo in (0, 37):
+        arrays = [rng.normal(size=n).astype(np.float32), np.full(n, np.nan, np.float32), np.full(n, np.nan, np.float32),
+                  (rng.normal(size=n) * 8).astype(np.float16), np.full(n, np.nan, np.float16),
+                  rng.integers(-128, 127, size=n).astype(np.int8), np.zeros(n, np.int8)]
+        _run_against_oracle(torch, kern, arrays, (lo,))

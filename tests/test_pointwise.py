@@ -109,6 +109,40 @@ def test_generated_cuda_compiles_for_sm100a(name):
     assert kern.spec.params["kernel"].build() > 0
 
 
+def test_vector_groups_only_where_four_points_are_contiguous():
+    """Which accesses the generic lowering turns into 4-point vector groups: unit stride in the
+    innermost T.Parallel variable, read-only loads, top-level stores to write-only tensors."""
+    n = 4096
+
+    @T.prim_func
+    def shapes(A: T.Tensor((n,), "float32"), B: T.Tensor((n,), "float32"), C: T.Tensor((n,), "float32"),
+               D: T.Tensor((64, 64), "float32"), E: T.Tensor((n,), "float32")):
+        with T.Kernel(T.ceildiv(n, 256), threads=128) as b:
+            for k in T.Parallel(256):
+                B[b * 256 + k] = A[b * 256 + k] * 2.0          # vector load and store
+                C[b * 256 + k] = C[b * 256 + k] + A[k * 2 % n]  # in place, stride 2: per point
+                D[b % 64, k % 64] = A[b * 256 + 1 + k]         # D per point; A a group (misaligned at run time)
+                acc = T.alloc_var("float32", 0)
+                for t in T.serial(3):
+                    acc += E[b * 256 + k + t]                   # depends on the loop: per point
+                if k > 3:
+                    E[b * 256 + k] = acc                        # E is read too: per point
+
+    src = ntilang.compile(shapes).get_cuda_source()
+    assert src.count("reinterpret_cast<const float4*>") == 2  # A[b*256 + k] and A[b*256 + 1 + k]
+    assert src.count("reinterpret_cast<float4*>") == 1  # B only
+    assert "(long long)threadIdx.x * 4" in src  # the 4-consecutive-points mapping
+
+    @T.prim_func
+    def odd_extent(A: T.Tensor((300,), "float32"), B: T.Tensor((300,), "float32")):
+        with T.Kernel(T.ceildiv(300, 30), threads=32) as b:
+            for k in T.Parallel(30):
+                B[b * 30 + k] = A[b * 30 + k] + 1.0
+
+    src = ntilang.compile(odd_extent).get_cuda_source()
+    assert "float4" not in src and "+ threadIdx.x;" in src  # 30 points: the strided mapping
+
+
 @needs_nvrtc
 def test_reference_examples_compile_on_the_generic_path():
     for name in ("fragment_affine", "piecewise", "window_sum"):
