@@ -533,7 +533,7 @@ class ClockSampler:
 # ----------------------------------------------------------------------------- measure
 
 
-def run_op(op, torch, dist, world, steps, warmup, stream, peaks, peak_kind, traffic, want_e2e):
+def run_op(op, torch, dist, world, steps, warmup, stream, peaks, peak_kind, traffic, want_e2e, want_call_path=True):
     from ntilang_b200 import _lib
 
     op.setup()
@@ -592,7 +592,8 @@ def run_op(op, torch, dist, world, steps, warmup, stream, peaks, peak_kind, traf
                      "traffic": tr.get("bytes_per_launch") if isinstance(tr, dict) else None,
                      "algorithmic_per_launch": units},
     }
-    result["python_call"] = measure_call_path(op, torch, stream)
+    if want_call_path:
+        result["python_call"] = measure_call_path(op, torch, stream)
     if want_e2e:
         result["e2e"] = measure_e2e(op, torch, dist, world, steps, stream)
     op.sets = None
@@ -838,6 +839,8 @@ def main():
     ap.add_argument("--ops", default=",".join(OPS))
     ap.add_argument("--cpu-seconds", type=float, default=2.0, help="CPU-baseline sample per op (0 = skip)")
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer end-to-end leg")
+    ap.add_argument("--no-call-path", action="store_true",
+                    help="skip the Python call-path timing (200 extra launches per op; for launch lists)")
     ap.add_argument("--gemm-shape", default=None, help="M,N,K override (profiling a small case)")
     ap.add_argument("--fa2-shape", default=None, help="B,H,S,D override (profiling a small case)")
     args = ap.parse_args()
@@ -938,7 +941,7 @@ def run_ours(args, ops):
         op = OPS[name](torch, device, rank)
         try:
             results[name] = run_op(op, torch, dist, world, args.steps, args.warmup, stream, peaks, peak_kind, traffic,
-                                   want_e2e=not args.no_e2e)
+                                   want_e2e=not args.no_e2e, want_call_path=not args.no_call_path)
         except _lib.KernelError as exc:
             if exc.code != 2:
                 raise
