@@ -70,6 +70,7 @@ struct GemmParams {
   int64_t sk_units;
   float* ws;             // sk_ctas partial-sum slots of BM x BN fp32
   uint32_t* flags;       // sk_ctas flags (0 = empty, 1 = partial ready)
+  int nar_pairs;         // CTA-pair kernel: pairs [0, nar_pairs) each take one column half of a tail tile
 };
 
 struct __align__(8) SharedCtl {
@@ -522,23 +523,35 @@ struct __align__(8) PairCtl {
 // into `split` = p.sk_units K-ranges over p.sk_ctas = (tiles - dp_tiles) * split pairs; in each
 // group of `split` consecutive pairs the highest one holds piece 0 (k-blocks from 0) and
 // finalises the tile, so every pair it waits for was launched before it.
+// Without a workspace the last partial wave's tiles are instead split along N: pair q of
+// [0, nar_pairs) computes columns [128 h, 128 h + 128) of tail tile dp_tiles + q / 2 (h = q % 2)
+// as a 256 x 128 MMA, so the tail takes half a tile's time and needs no partial sums.
 struct PairWork {
   int tile, k0, k1;
   int piece;  // 0: data-parallel or finaliser; > 0: contributor
   int slot;   // first workspace slot of this tile's contributors (split tiles only)
+  int half;   // -1: all BN columns; 0 / 1: that 128-column half (N-split tail tile)
 };
 
 struct PairIter {
   int t;
-  bool split_left;
+  bool split_left, narrow_left;
   __device__ __forceinline__ void init(const GemmParams& p, int pair) {
     t = pair;
     split_left = pair < p.sk_ctas;
+    narrow_left = pair < p.nar_pairs;
   }
   __device__ __forceinline__ bool next(const GemmParams& p, int pair, int num_pairs, PairWork& w) {
+    w.half = -1;
     if (t < p.dp_tiles) {
       w.tile = t, w.k0 = 0, w.k1 = p.kb, w.piece = 0, w.slot = 0;
       t += num_pairs;
+      return true;
+    }
+    if (narrow_left) {
+      narrow_left = false;
+      w.tile = p.dp_tiles + pair / 2, w.half = pair % 2;
+      w.k0 = 0, w.k1 = p.kb, w.piece = 0, w.slot = 0;
       return true;
     }
     if (split_left) {
@@ -555,6 +568,25 @@ struct PairIter {
     return false;
   }
 };
+
+// Bytes one CTA's copies bring into a stage for work item w: A rows plus the CTA's B columns
+// (64 instead of 128 for the half tile of a row-major B; a [N, K] B box is always 128 rows).
+__device__ __forceinline__ uint32_t pair_half_bytes(const GemmParams& p, const PairWork& w) {
+  return (w.half >= 0 && !p.b_trans) ? PR_A_STAGE + PR_B_STAGE / 2 : PR_STAGE_BYTES;
+}
+
+// The same for the pair's stage-load sequence number `seq` (walks the work list; abort path only).
+__device__ uint32_t pair_seq_half_bytes(const GemmParams& p, int pair, int num_pairs, int seq) {
+  PairIter it;
+  it.init(p, pair);
+  PairWork w;
+  int base = 0;
+  while (it.next(p, pair, num_pairs, w)) {
+    if (seq < base + (w.k1 - w.k0)) return pair_half_bytes(p, w);
+    base += w.k1 - w.k0;
+  }
+  return PR_STAGE_BYTES;
+}
 
 __device__ __forceinline__ void pair_abort(PairCtl* ctl, uint32_t code) {
   atomicCAS(&g_gemm_status, 0u, code);
@@ -620,7 +652,12 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_pair_kernel(const __grid_cons
         int mb, nb;
         tile_coords(w.tile, p.num_m, p.num_n, mb, nb);
         const int m0 = mb * PR_TILE_M + static_cast<int>(rank) * PR_BM;
-        const int n0 = nb * BN + static_cast<int>(rank) * PR_BN_HALF;
+        // Each CTA holds half of the tile's B columns: 128 of a full tile, 64 of a half tile
+        // (a [N, K] B is fetched as a 128-row box either way; the MMA reads the first 64).
+        const int n0 = w.half < 0 ? nb * BN + static_cast<int>(rank) * PR_BN_HALF
+                                  : nb * BN + w.half * PR_BN_HALF + static_cast<int>(rank) * (PR_BN_HALF / 2);
+        const uint32_t half_bytes = pair_half_bytes(p, w);
+        const int b_boxes = w.half < 0 ? PR_BN_HALF / 64 : 1;  // 64-column boxes of a row-major B
         bool ok = true;
         for (int kb = w.k0; kb < w.k1; ++kb) {
           if (!mbar_wait_bounded(&ctl->empty[stage], phase ^ 1, p.wait_limit, abort_flag)) {
@@ -629,15 +666,14 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_pair_kernel(const __grid_cons
             break;
           }
           const uint32_t full_addr = mapa_shared(smem_u32(&ctl->full[stage]), 0);
-          if (rank == 0) mbar_arrive_expect_tx(&ctl->full[stage], 2 * PR_STAGE_BYTES);
+          if (rank == 0) mbar_arrive_expect_tx(&ctl->full[stage], 2 * half_bytes);
           uint8_t* a_dst = sA + stage * PR_A_STAGE;
           uint8_t* b_dst = sB + stage * PR_B_STAGE;
           tma_load_2d_pair(a_dst, &tmap_a, full_addr, kb * BK, m0);
           if (p.b_trans) {
             tma_load_2d_pair(b_dst, &tmap_b, full_addr, kb * BK, n0);
           } else {
-#pragma unroll
-            for (int i = 0; i < PR_BN_HALF / 64; ++i)
+            for (int i = 0; i < b_boxes; ++i)
               tma_load_2d_pair(b_dst + i * (64 * BK * 2), &tmap_b, full_addr, n0 + i * 64, kb * BK);
           }
           ++issued;
@@ -651,7 +687,8 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_pair_kernel(const __grid_cons
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer (rank 0)
     if (rank == 0 && elect_one_lane()) {
-      const uint32_t idesc = umma_idesc_f16_f32(PR_TILE_M, BN, 0, p.b_trans ? 0 : 1);
+      const uint32_t idesc_full = umma_idesc_f16_f32(PR_TILE_M, BN, 0, p.b_trans ? 0 : 1);
+      const uint32_t idesc_half = umma_idesc_f16_f32(PR_TILE_M, BN / 2, 0, p.b_trans ? 0 : 1);
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
@@ -668,6 +705,7 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_pair_kernel(const __grid_cons
         }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * BN;
+        const uint32_t idesc = w.half < 0 ? idesc_full : idesc_half;
         for (int kb = w.k0; kb < w.k1; ++kb) {
           if (!mbar_wait_bounded(&ctl->full[stage], phase, p.wait_limit, abort_flag)) {
             if (!*abort_flag) pair_abort(ctl, NTL_STATUS_MMA_FULL_WAIT);
@@ -768,9 +806,11 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_pair_kernel(const __grid_cons
       float* crow = p.c + static_cast<int64_t>(row) * p.N;
       const float row_bias = (p.bias_mode == NTL_BIAS_M && row_ok) ? __ldg(p.bias + row) : 0.0f;
       float* bias_s = reinterpret_cast<float*>(smem + PR_STAGES * PR_STAGE_BYTES + 1024) + (warp - 2) * BN;
-      if (p.bias_mode == NTL_BIAS_N) stage_bias_n(p, nb * BN, bias_s, lane);
-      for (int chunk = 0; chunk < BN / 32; ++chunk) {
-        const int col0 = nb * BN + chunk * 32;
+      const int ncol0 = nb * BN + (w.half < 0 ? 0 : w.half * PR_BN_HALF);
+      const int nchunks = (w.half < 0 ? BN : PR_BN_HALF) / 32;
+      if (p.bias_mode == NTL_BIAS_N) stage_bias_n(p, ncol0, bias_s, lane);
+      for (int chunk = 0; chunk < nchunks; ++chunk) {
+        const int col0 = ncol0 + chunk * 32;
         if (col0 >= p.N) break;
         uint32_t r[32];
         tmem_ld_32x32b_x32(t_lane + acc * BN + chunk * 32, r);
@@ -821,8 +861,9 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_pair_kernel(const __grid_cons
     for (int i = hi > PR_STAGES ? hi - PR_STAGES : 0; i < hi; ++i) {
       const int s = i % PR_STAGES;
       const uint32_t ph = static_cast<uint32_t>(i / PR_STAGES) & 1u;
-      if (i >= own) mbar_arrive_expect_tx(&ctl->full[s], PR_STAGE_BYTES);
-      else if (i >= peer) mbar_complete_tx(&ctl->full[s], PR_STAGE_BYTES);
+      const uint32_t half_bytes = pair_seq_half_bytes(p, pair, num_pairs, i);
+      if (i >= own) mbar_arrive_expect_tx(&ctl->full[s], half_bytes);
+      else if (i >= peer) mbar_complete_tx(&ctl->full[s], half_bytes);
       if (!mbar_wait_bounded(&ctl->full[s], ph, int64_t(1) << 24, nullptr))
         atomicCAS(&g_gemm_status, 0u, NTL_STATUS_DRAIN_WAIT);
     }
@@ -971,7 +1012,7 @@ int pair_clusters(int* clusters_out) {
 // Work plan of the pair kernel.  With a workspace, the tiles of the last partial wave are
 // split along K over the otherwise idle pairs (2 to 4 pieces of at least 4 k-blocks each).
 struct PairPlan {
-  int num_m, num_n, tiles, kb, pairs, dp_tiles, split, split_pairs;
+  int num_m, num_n, tiles, kb, pairs, dp_tiles, split, split_pairs, nar_pairs;
   size_t ws_bytes;
 };
 
@@ -990,8 +1031,17 @@ int make_pair_plan(int64_t M, int64_t N, int64_t K, bool split_tail, PairPlan* p
   pl->dp_tiles = pl->tiles;
   pl->split = 1;
   pl->split_pairs = 0;
+  pl->nar_pairs = 0;
   pl->ws_bytes = 0;
   const int left = pl->tiles % clusters;
+  if (!split_tail && left > 0 && 2 * left <= clusters) {
+    // The partial wave's tiles become 2 x `left` half tiles on otherwise idle pairs (with
+    // fewer tiles than half the pairs, every tile is split and twice as many pairs work).
+    pl->pairs = pl->tiles > clusters ? clusters : 2 * left;
+    pl->dp_tiles = pl->tiles - left;
+    pl->nar_pairs = 2 * left;
+    return NTL_OK;
+  }
   if (split_tail && left > 0) {
     int split = clusters / left;
     if (split > PR_MAX_SPLIT) split = PR_MAX_SPLIT;
@@ -1022,6 +1072,7 @@ int gemm_pair_launch(const uint16_t* a, const uint16_t* b, GemmParams p, void* w
   p.dp_tiles = pl.dp_tiles;
   p.sk_ctas = pl.split_pairs;
   p.sk_units = pl.split;
+  p.nar_pairs = pl.nar_pairs;
   p.ws = pl.split > 1 ? reinterpret_cast<float*>(static_cast<unsigned char*>(ws) + kWsFlagBytes) : nullptr;
   p.flags = pl.split > 1 ? static_cast<uint32_t*>(ws) : nullptr;
   CUtensorMap ma, mb;
@@ -1095,6 +1146,7 @@ int gemm_launch(const uint16_t* a, const uint16_t* b, float* c, const float* bia
   if (M == 0 || N == 0) return NTL_OK;
   NTL_REQUIRE(c && (K == 0 || (a && b)), NTL_ERR_INVALID, "gemm: NULL pointer");
   GemmParams p;
+  p.nar_pairs = 0;
   p.c = c;
   p.bias = bias;
   p.bias_mode = bias_mode;

@@ -227,3 +227,34 @@ def test_gemm_workspace_too_small_is_rejected(torch_cuda):
     with pytest.raises(_lib.KernelError, match="workspace"):
         _lib.call("ntl_gemm_f16_f32_ws", a.data_ptr(), b.data_ptr(), c.data_ptr(), None, 0, 1.0, 0, m, n, k, 0,
                   ws.data_ptr(), ws.numel(), torch.cuda.current_stream().cuda_stream)
+
+
+@pytest.mark.parametrize("m,n,k,trans_b,bias_mode", [
+    (2560, 4096, 512, 0, 1),   # 160 pair tiles: two full waves on 74 pairs, 12 tail tiles split along N
+    (2560, 4096, 512, 1, 3),   # the same with B given as [N, K] and a per-row bias
+    (1536, 1000, 264, 1, 1),   # 24 tiles, all split; ragged N: the last tile's second half is empty
+    (1536, 1000, 264, 0, 0),
+    (384, 520, 136, 0, 1),     # 6 tiles on 12 pairs, ragged M / N / K
+])
+def test_gemm_n_split_tail_tiles(torch_cuda, m, n, k, trans_b, bias_mode):
+    """Data-parallel entry: the last partial wave's 256x256 tiles run as two 256x128 halves on
+    otherwise idle CTA pairs (every tile when there are fewer tiles than half the pairs)."""
+    torch = torch_cuda
+    from ntilang_b200 import _lib
+
+    gen = torch.Generator(device="cuda").manual_seed(m + n)
+    a = (torch.randn(m, k, device="cuda", generator=gen) / k**0.5).half()
+    b = torch.randn(n, k, device="cuda", generator=gen).half() if trans_b else \
+        torch.randn(k, n, device="cuda", generator=gen).half()
+    bias = torch.randn(m if bias_mode == 3 else n, device="cuda", generator=gen)
+    ref = ref_gemm(torch, a, b, trans_b=bool(trans_b)) * 0.75
+    if bias_mode == 1:
+        ref = ref + bias[None, :]
+    elif bias_mode == 3:
+        ref = ref + bias[:, None]
+    ref = torch.relu(ref)
+    for _ in range(2):
+        c = torch.full((m, n), float("nan"), device="cuda")
+        _lib.call("ntl_gemm_f16_f32", a.data_ptr(), b.data_ptr(), c.data_ptr(), bias.data_ptr(), bias_mode, 0.75, 1,
+                  m, n, k, trans_b, torch.cuda.current_stream().cuda_stream)
+        check(torch, c, ref)
