@@ -23,7 +23,7 @@ namespace {
 constexpr unsigned kFull = 0xffffffffu;
 // Rows (warps) per block of the warp-per-row kernels, measured per op on B200 at the BASELINE
 // shapes: softmax 16384x512 is fastest with 8, RMSNorm 4096x1024 with 16 (6.4 vs 6.8 us).
-constexpr int kSoftmaxWarpsPerBlock = 8;
+constexpr int kSoftmaxWarpsPerBlock = 4;
 constexpr int kRmsnormWarpsPerBlock = 16;
 constexpr int kLayernormWarpsPerBlock = 16;
 
