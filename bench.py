@@ -676,7 +676,7 @@ def cpu_baseline(op, seconds):
 
 # ------------------------------------------------------------------------------ the reference's kernels on the GPU
 
-REF_INSTALL = ROOT / "baseline" / "_ref"
+REF_INSTALL = Path(os.environ.get("NTL_REFERENCE_DIR", str(ROOT / "baseline" / "_ref")))
 
 
 def reference_builders(target):
