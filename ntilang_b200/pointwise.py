@@ -392,9 +392,9 @@ class _Lowering:
             d = self._vec_deps(e)
             if d is None or not d <= free or inner in d:
                 return False
-        if self.dtype(idx[-1]) not in ("int32", "int64", "uint32", "uint64"):
-            return False
-        return self._unit_stride(idx[-1], inner, free)
+        # the shape test first: it rejects indices holding loads, whose code generation would emit
+        return self._unit_stride(idx[-1], inner, free) and self.dtype(idx[-1]) in ("int32", "int64", "uint32",
+                                                                                   "uint64")
 
     def _unit_stride(self, e, inner, free) -> bool:
         """``e`` is ``inner`` plus / minus terms free of it, through + and - only.  Wrapping
