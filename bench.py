@@ -3,14 +3,16 @@
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference|reference-gpu] [--ops a,b,...]
 
-A *step* is one launch of an op over one batch of synthetic input with BASELINE.json's
-shapes and distributions.  The headline line is the configuration BASELINE.json's metric
-is normally quoted on (configs[1]: row cumsum, X f32 [32768, 256]); every op family's
-measurement is in the same line under ``"ops"``.
+A *step* is one pass of an op over one batch of synthetic input with BASELINE.json's
+shapes and distributions.  The headline is the configuration BASELINE.json's metric is
+normally quoted on (configs[1]: row cumsum, X f32 [32768, 256]); every op family's figures
+are in the same line under ``"ops"`` (value, roofline fraction, ms per step, end-to-end and
+CPU baselines), and the full per-op records go to a side file the line names.
 
 value      K steps replayed from one CUDA graph (inputs resident in HBM, rotated over
-           enough buffer sets that the working set exceeds L2 between reuses), timed with
-           CUDA events on the launching stream between barriers; max over ranks.
+           enough buffer sets that no set is reused within 3x L2 of other traffic, L2
+           flushed before the timed replay), timed with CUDA events on the launching
+           stream between barriers; max over ranks.
 e2e        the same metric through the public call (``CompiledKernel.__call__`` -> C ABI)
            with pinned host buffers: every step copies its inputs host->device and its
            output device->host inside the timed region (steps alternate between two
@@ -18,9 +20,15 @@ e2e        the same metric through the public call (``CompiledKernel.__call__`` 
 roofline   algorithmic bytes (or FLOPs) per launch / average launch time, against the
            measured HBM copy bandwidth or dense bf16 GEMM rate in MEASURED_PEAKS.json.
 cpu_baseline  the CPU oracle (a restatement of the reference's algorithm; ``kind: port``)
-           on the host cores, bounded sample, rank 0 at N=1 only.
-Multi-GPU: each rank runs a full config-sized shard of an N-times larger job (row blocks,
-M-panels or (batch, head) slices; no collective on the data path): ``scaling: weak``.
+           on the host cores, bounded sample, rank 0 at N=1 only; beside it the same op in
+           torch on all host cores (``cpu_torch``).
+Multi-GPU (``scaling: strong``): one BASELINE job is split across the N ranks -- contiguous
+row blocks for the row ops, M-panels of A and C (B and bias replicated) for the GEMMs,
+batches of (batch, head) pairs for attention -- with no collective on the data path.  The
+value is the whole job's algorithmic work / the slowest rank's time per step.  After the
+timed region the shards' outputs are all-gathered over NCCL and rank 0 compares them
+bit-for-bit with the same kernels run on the whole job on one GPU.  ``weak`` repeats the
+timing with a full-size job on every rank.
 """
 
 from __future__ import annotations
@@ -41,6 +49,7 @@ BASELINE_METRIC = "achieved GB/s or TFLOPS per op at 1/2/4/8 B200 and % of HBM/t
 HEADLINE = "cumsum"
 L2_BYTES = 126 * 1024 * 1024
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+DETAIL_DEFAULT = "gpurun_out/bench_detail_n{n}.json"
 
 
 def load_peaks():
@@ -61,247 +70,369 @@ def load_traffic():
     return {}
 
 
+def cpu_model() -> str:
+    try:
+        for line in Path("/proc/cpuinfo").read_text().splitlines():
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    import platform
+
+    return platform.processor() or "unknown"
+
+
+def shard_bounds(total, rank, world):
+    from ntilang_b200.dist import shard_bounds as bounds
+
+    return bounds(total, rank, world)
+
+
 # ---------------------------------------------------------------------------- workloads
 
 
 class Op:
+    """One bench workload.  ``world`` > 1 makes this rank's instance a shard of the job."""
+
     name = ""
     bound = "hbm"
     unit = "GB/s"
     dtype = "f32"
 
-    def __init__(self, torch, device, rank):
-        self.torch, self.device, self.rank = torch, device, rank
+    def __init__(self, torch, device, rank=0, world=1):
+        self.torch, self.device, self.rank, self.world = torch, device, rank, world
+        self.localize()
+
+    def localize(self):
+        """Set this rank's share of the job."""
 
     def sets_needed(self, footprint):
-        return max(1, min(8, math.ceil(3 * L2_BYTES / max(1, footprint))))
+        """Distinct buffer sets so that a set is reused only after > 3x L2 of other traffic
+        (bounded to about 2 GiB of buffers)."""
+        want = math.ceil(3 * L2_BYTES / max(1, footprint))
+        cap = max(1, (2 << 30) // max(1, footprint))
+        return max(1, min(want, cap, 256))
 
-    def units(self):  # algorithmic bytes or FLOPs per step
-        raise NotImplementedError
+    def units(self):  # algorithmic bytes or FLOPs of this rank's share, per step
+        return self.units_of_rank(self.rank)
+
+    def units_of_rank(self, r):
+        return self.units_of_rows(self.rows_of_rank(r))
+
+    def whole_job_units(self):  # the job on one GPU (what the ncu captures cover)
+        return self.units_of_rows(self.full_rows)
+
+    def total_units(self):  # of the whole job (all ranks), per step
+        return sum(self.units_of_rank(r) for r in range(self.world))
 
     def per_unit(self):
         return 1e9 if self.unit == "GB/s" else 1e12
 
+    def g(self, seed):
+        return self.torch.Generator(device=self.device).manual_seed(seed)
+
+    # -- the generic setup: set 0 is this rank's slice of one seeded global input (so the
+    # gathered outputs can be checked against a one-GPU run of the whole job); the other
+    # sets are independent local inputs.
+    def setup(self):
+        self.kernel = self.make_kernel(local=True)
+        ins0 = self.slice_inputs(self.global_inputs())
+        foot = sum(t.numel() * t.element_size() for t in ins0) + self.out_bytes(ins0)
+        self.sets = []
+        for s in range(self.sets_needed(foot)):
+            ins = ins0 if s == 0 else self.local_inputs(s)
+            out = self.alloc_out(ins)
+            self.sets.append((ins + (out,), ins, out))
+
+    def out_bytes(self, ins):
+        return ins[0].numel() * 4
+
+    def alloc_out(self, ins):
+        return self.torch.empty_like(ins[0])
+
+    def gather_view(self, y):  # the rank's output as rows of the shard axis
+        return y
+
+    def ungather(self, g):
+        return g
+
 
 class RowOp(Op):
+    full_rows = cols = 0
+
+    def localize(self):
+        b, e = shard_bounds(self.full_rows, self.rank, self.world)
+        self.r0, self.rows = b, e - b
+
+    def rows_of_rank(self, r):
+        b, e = shard_bounds(self.full_rows, r, self.world)
+        return e - b
+
     def gen(self, shape, dist, seed):
         torch = self.torch
-        g = torch.Generator(device=self.device).manual_seed(seed)
+        g = self.g(seed)
         if dist == "uniform":
             return torch.rand(shape, device=self.device, generator=g) * 2 - 1
         return torch.randn(shape, device=self.device, generator=g) * dist
 
+    def take(self, x):
+        return x[self.r0:self.r0 + self.rows].contiguous()
+
 
 class RMSNormOp(RowOp):
     name = "rmsnorm"
-    rows, cols, eps = 4096, 1024, 1e-6
+    full_rows, cols, eps = 4096, 1024, 1e-6
     config = "RMSNorm X f32 [4096,1024] ~N(0,1), gamma f32 [1024] ~N(1,0.1), eps 1e-6"
 
-    def setup(self):
+    def units_of_rows(self, rows):
+        return 2 * rows * self.cols * 4 + self.cols * 4
+
+    def make_kernel(self, local):
         from ntilang_b200 import kernels as K
 
-        self.kernel = K.rmsnorm(self.rows, self.cols, self.eps)
-        n = self.sets_needed(2 * self.rows * self.cols * 4)
-        self.sets = []
-        for s in range(n):
-            x = self.gen((self.rows, self.cols), 1.0, 1000 * self.rank + s)
-            w = self.gen((self.cols,), 0.1, 7 + s) + 1.0
-            y = self.torch.empty_like(x)
-            self.sets.append(((x, w, y), (x, w), y))
+        return K.rmsnorm(self.rows if local else self.full_rows, self.cols, self.eps)
 
-    def units(self):
-        return 2 * self.rows * self.cols * 4 + self.cols * 4
+    def global_inputs(self):
+        return self.gen((self.full_rows, self.cols), 1.0, 0), self.gen((self.cols,), 0.1, 7) + 1.0
+
+    def slice_inputs(self, full):
+        return self.take(full[0]), full[1]
+
+    def local_inputs(self, s):
+        return self.gen((self.rows, self.cols), 1.0, 1000 * self.rank + s), self.gen((self.cols,), 0.1, 7 + s) + 1.0
 
     def cpu(self, seconds):
         import numpy as np
 
         from oracle import rowops
 
-        rows = 1024
+        rows = self.full_rows
         x = np.random.default_rng(0).normal(size=(rows, self.cols)).astype(np.float32)
         w = np.random.default_rng(1).normal(1, 0.1, size=self.cols).astype(np.float32)
-        n, t0 = 0, time.perf_counter()
-        while time.perf_counter() - t0 < seconds:
-            rowops.rmsnorm(x, w, self.eps)
-            n += 1
-        dt = time.perf_counter() - t0
-        return n * (2 * rows * self.cols * 4 + self.cols * 4) / dt / 1e9, f"{n} x RMSNorm [{rows},{self.cols}]"
+        return timed(lambda: rowops.rmsnorm(x, w, self.eps), seconds,
+                     2 * rows * self.cols * 4 + self.cols * 4, 1e9, f"RMSNorm [{rows},{self.cols}]")
+
+    def cpu_torch(self, torch, seconds):
+        rows = self.full_rows
+        g = torch.Generator().manual_seed(0)
+        x = torch.randn(rows, self.cols, generator=g)
+        w = torch.randn(self.cols, generator=g) * 0.1 + 1
+
+        def run():
+            return x * torch.rsqrt((x * x).mean(dim=1, keepdim=True) + self.eps) * w
+
+        return timed(run, seconds, 2 * rows * self.cols * 4 + self.cols * 4, 1e9, f"RMSNorm [{rows},{self.cols}]")
 
 
 class LayerNormOp(RowOp):
     name = "layernorm"
-    rows, cols, eps = 4096, 1024, 1e-5
-    config = "LayerNorm X f32 [4096,1024] ~N(0,1), gamma f32 [1024] ~N(1,0.1), beta f32 [1024] ~N(0,0.1), eps 1e-5"
+    full_rows, cols, eps = 4096, 1024, 1e-5
+    config = "LayerNorm X f32 [4096,1024] ~N(0,1), gamma ~N(1,0.1), beta ~N(0,0.1), eps 1e-5"
 
-    def setup(self):
+    def units_of_rows(self, rows):
+        return 2 * rows * self.cols * 4 + 2 * self.cols * 4
+
+    def make_kernel(self, local):
         from ntilang_b200 import kernels as K
 
-        self.kernel = K.layernorm(self.rows, self.cols, self.eps)
-        n = self.sets_needed(2 * self.rows * self.cols * 4)
-        self.sets = []
-        for s in range(n):
-            x = self.gen((self.rows, self.cols), 1.0, 1000 * self.rank + s)
-            w = self.gen((self.cols,), 0.1, 7 + s) + 1.0
-            b = self.gen((self.cols,), 0.1, 17 + s)
-            y = self.torch.empty_like(x)
-            self.sets.append(((x, w, b, y), (x, w, b), y))
+        return K.layernorm(self.rows if local else self.full_rows, self.cols, self.eps)
 
-    def units(self):
-        return 2 * self.rows * self.cols * 4 + 2 * self.cols * 4
+    def global_inputs(self):
+        return (self.gen((self.full_rows, self.cols), 1.0, 0), self.gen((self.cols,), 0.1, 7) + 1.0,
+                self.gen((self.cols,), 0.1, 17))
+
+    def slice_inputs(self, full):
+        return self.take(full[0]), full[1], full[2]
+
+    def local_inputs(self, s):
+        return (self.gen((self.rows, self.cols), 1.0, 1000 * self.rank + s), self.gen((self.cols,), 0.1, 7 + s) + 1.0,
+                self.gen((self.cols,), 0.1, 17 + s))
 
     def cpu(self, seconds):
         import numpy as np
 
         from oracle import rowops
 
-        rows = 1024
+        rows = self.full_rows
         x = np.random.default_rng(0).normal(size=(rows, self.cols)).astype(np.float32)
         w = np.random.default_rng(1).normal(1, 0.1, size=self.cols).astype(np.float32)
         b = np.random.default_rng(2).normal(0, 0.1, size=self.cols).astype(np.float32)
-        n, t0 = 0, time.perf_counter()
-        while time.perf_counter() - t0 < seconds:
-            rowops.layernorm(x, w, b, self.eps)
-            n += 1
-        dt = time.perf_counter() - t0
-        return n * (2 * rows * self.cols * 4 + 2 * self.cols * 4) / dt / 1e9, f"{n} x LayerNorm [{rows},{self.cols}]"
+        return timed(lambda: rowops.layernorm(x, w, b, self.eps), seconds,
+                     2 * rows * self.cols * 4 + 2 * self.cols * 4, 1e9, f"LayerNorm [{rows},{self.cols}]")
+
+    def cpu_torch(self, torch, seconds):
+        rows = self.full_rows
+        g = torch.Generator().manual_seed(0)
+        x = torch.randn(rows, self.cols, generator=g)
+        w = torch.randn(self.cols, generator=g) * 0.1 + 1
+        b = torch.randn(self.cols, generator=g) * 0.1
+        return timed(lambda: torch.nn.functional.layer_norm(x, (self.cols,), w, b, self.eps), seconds,
+                     2 * rows * self.cols * 4 + 2 * self.cols * 4, 1e9, f"LayerNorm [{rows},{self.cols}]")
 
 
 class TransposeOp(RowOp):
+    """A [m, n] -> B [n, m]; a rank transposes a block of A's rows into its own [n, m/N] block."""
+
     name = "transpose"
-    m, n = 4096, 4096
+    full_rows, cols = 4096, 4096
     config = "shared transpose A f32 [4096,4096] ~N(0,1) -> B [4096,4096] (README config)"
 
-    def setup(self):
+    def units_of_rows(self, rows):
+        return 2 * rows * self.cols * 4
+
+    def make_kernel(self, local):
         from ntilang_b200 import kernels as K
 
-        self.kernel = K.transpose(self.m, self.n)
-        k = self.sets_needed(2 * self.m * self.n * 4)
-        self.sets = []
-        for s in range(k):
-            a = self.gen((self.m, self.n), 1.0, 1000 * self.rank + s)
-            b = self.torch.empty((self.n, self.m), device=self.device)
-            self.sets.append(((a, b), (a,), b))
+        return K.transpose(self.rows if local else self.full_rows, self.cols)
 
-    def units(self):
-        return 2 * self.m * self.n * 4
+    def global_inputs(self):
+        return (self.gen((self.full_rows, self.cols), 1.0, 0),)
+
+    def slice_inputs(self, full):
+        return (self.take(full[0]),)
+
+    def local_inputs(self, s):
+        return (self.gen((self.rows, self.cols), 1.0, 1000 * self.rank + s),)
+
+    def alloc_out(self, ins):
+        return self.torch.empty((self.cols, ins[0].shape[0]), device=self.device)
+
+    def gather_view(self, y):
+        return y.t().contiguous()
+
+    def ungather(self, g):
+        return g.t()
 
     def cpu(self, seconds):
         import numpy as np
 
         from oracle import rowops
 
-        m = 1024
-        a = np.random.default_rng(0).normal(size=(m, self.n)).astype(np.float32)
-        k, t0 = 0, time.perf_counter()
-        while time.perf_counter() - t0 < seconds:
-            rowops.transpose(a)
-            k += 1
-        dt = time.perf_counter() - t0
-        return k * 2 * m * self.n * 4 / dt / 1e9, f"{k} x transpose [{m},{self.n}]"
+        m = self.full_rows
+        a = np.random.default_rng(0).normal(size=(m, self.cols)).astype(np.float32)
+        return timed(lambda: rowops.transpose(a), seconds, 2 * m * self.cols * 4, 1e9, f"transpose [{m},{self.cols}]")
+
+    def cpu_torch(self, torch, seconds):
+        m = self.full_rows
+        a = torch.randn(m, self.cols, generator=torch.Generator().manual_seed(0))
+        return timed(lambda: a.t().contiguous(), seconds, 2 * m * self.cols * 4, 1e9, f"transpose [{m},{self.cols}]")
 
 
 class CumsumOp(RowOp):
     name = "cumsum"
-    rows, cols = 32768, 256
+    full_rows, cols = 32768, 256
     config = "row inclusive cumsum X f32 [32768,256] ~U(-1,1)"
 
-    def setup(self):
+    def units_of_rows(self, rows):
+        return 2 * rows * self.cols * 4
+
+    def make_kernel(self, local):
         from ntilang_b200 import kernels as K
 
-        self.kernel = K.cumsum(self.rows, self.cols)
-        n = self.sets_needed(2 * self.rows * self.cols * 4)
-        self.sets = []
-        for s in range(n):
-            x = self.gen((self.rows, self.cols), "uniform", 1000 * self.rank + s)
-            y = self.torch.empty_like(x)
-            self.sets.append(((x, y), (x,), y))
+        return K.cumsum(self.rows if local else self.full_rows, self.cols)
 
-    def units(self):
-        return 2 * self.rows * self.cols * 4
+    def global_inputs(self):
+        return (self.gen((self.full_rows, self.cols), "uniform", 0),)
+
+    def slice_inputs(self, full):
+        return (self.take(full[0]),)
+
+    def local_inputs(self, s):
+        return (self.gen((self.rows, self.cols), "uniform", 1000 * self.rank + s),)
 
     def cpu(self, seconds):
         import numpy as np
 
         from oracle import rowops
 
-        rows = 4096
+        rows = self.full_rows
         x = np.random.default_rng(0).uniform(-1, 1, size=(rows, self.cols)).astype(np.float32)
-        n, t0 = 0, time.perf_counter()
-        while time.perf_counter() - t0 < seconds:
-            rowops.cumsum(x)
-            n += 1
-        dt = time.perf_counter() - t0
-        return n * 2 * rows * self.cols * 4 / dt / 1e9, f"{n} x cumsum [{rows},{self.cols}]"
+        return timed(lambda: rowops.cumsum(x), seconds, 2 * rows * self.cols * 4, 1e9, f"cumsum [{rows},{self.cols}]")
+
+    def cpu_torch(self, torch, seconds):
+        rows = self.full_rows
+        x = torch.rand(rows, self.cols, generator=torch.Generator().manual_seed(0)) * 2 - 1
+        return timed(lambda: torch.cumsum(x, dim=1), seconds, 2 * rows * self.cols * 4, 1e9,
+                     f"cumsum [{rows},{self.cols}]")
 
 
 class SoftmaxOp(RowOp):
     name = "softmax"
-    rows, cols = 16384, 512
+    full_rows, cols = 16384, 512
     config = "row softmax X f32 [16384,512] ~N(0,4)"
 
-    def setup(self):
+    def units_of_rows(self, rows):
+        return 2 * rows * self.cols * 4
+
+    def make_kernel(self, local):
         from ntilang_b200 import kernels as K
 
-        self.kernel = K.softmax(self.rows, self.cols)
-        n = self.sets_needed(2 * self.rows * self.cols * 4)
-        self.sets = []
-        for s in range(n):
-            x = self.gen((self.rows, self.cols), 2.0, 1000 * self.rank + s)
-            y = self.torch.empty_like(x)
-            self.sets.append(((x, y), (x,), y))
+        return K.softmax(self.rows if local else self.full_rows, self.cols)
 
-    def units(self):
-        return 2 * self.rows * self.cols * 4
+    def global_inputs(self):
+        return (self.gen((self.full_rows, self.cols), 2.0, 0),)
+
+    def slice_inputs(self, full):
+        return (self.take(full[0]),)
+
+    def local_inputs(self, s):
+        return (self.gen((self.rows, self.cols), 2.0, 1000 * self.rank + s),)
 
     def cpu(self, seconds):
         import numpy as np
 
         from oracle import rowops
 
-        rows = 2048
+        rows = self.full_rows
         x = (np.random.default_rng(0).normal(size=(rows, self.cols)) * 2).astype(np.float32)
-        n, t0 = 0, time.perf_counter()
-        while time.perf_counter() - t0 < seconds:
-            rowops.softmax(x)
-            n += 1
-        dt = time.perf_counter() - t0
-        return n * 2 * rows * self.cols * 4 / dt / 1e9, f"{n} x softmax [{rows},{self.cols}]"
+        return timed(lambda: rowops.softmax(x), seconds, 2 * rows * self.cols * 4, 1e9, f"softmax [{rows},{self.cols}]")
+
+    def cpu_torch(self, torch, seconds):
+        rows = self.full_rows
+        x = torch.randn(rows, self.cols, generator=torch.Generator().manual_seed(0)) * 2
+        return timed(lambda: torch.softmax(x, dim=1), seconds, 2 * rows * self.cols * 4, 1e9,
+                     f"softmax [{rows},{self.cols}]")
 
 
 class VaddOp(RowOp):
     name = "vadd"
-    n = 16 * 1024 * 1024
+    full_rows, cols = 16 * 1024 * 1024, 1
     config = "vector add A,B f32 [16777216] ~N(0,1)"
 
-    def setup(self):
+    def units_of_rows(self, rows):
+        return 3 * rows * 4
+
+    def make_kernel(self, local):
         from ntilang_b200 import kernels as K
 
-        self.kernel = K.vector_add(self.n)
-        k = self.sets_needed(3 * self.n * 4)
-        self.sets = []
-        for s in range(k):
-            a = self.gen((self.n,), 1.0, 1000 * self.rank + 2 * s)
-            b = self.gen((self.n,), 1.0, 1000 * self.rank + 2 * s + 1)
-            c = self.torch.empty_like(a)
-            self.sets.append(((a, b, c), (a, b), c))
+        return K.vector_add(self.rows if local else self.full_rows)
 
-    def units(self):
-        return 3 * self.n * 4
+    def global_inputs(self):
+        return self.gen((self.full_rows,), 1.0, 0), self.gen((self.full_rows,), 1.0, 1)
+
+    def slice_inputs(self, full):
+        return self.take(full[0]), self.take(full[1])
+
+    def local_inputs(self, s):
+        return (self.gen((self.rows,), 1.0, 1000 * self.rank + 2 * s),
+                self.gen((self.rows,), 1.0, 1000 * self.rank + 2 * s + 1))
 
     def cpu(self, seconds):
         import numpy as np
 
         from oracle import rowops
 
-        m = 4 * 1024 * 1024
+        m = self.full_rows
         a = np.random.default_rng(0).normal(size=m).astype(np.float32)
         b = np.random.default_rng(1).normal(size=m).astype(np.float32)
-        n, t0 = 0, time.perf_counter()
-        while time.perf_counter() - t0 < seconds:
-            rowops.vadd(a, b)
-            n += 1
-        dt = time.perf_counter() - t0
-        return n * 3 * m * 4 / dt / 1e9, f"{n} x vector add [{m}]"
+        return timed(lambda: rowops.vadd(a, b), seconds, 3 * m * 4, 1e9, f"vector add [{m}]")
+
+    def cpu_torch(self, torch, seconds):
+        m = self.full_rows
+        g = torch.Generator().manual_seed(0)
+        a, b = torch.randn(m, generator=g), torch.randn(m, generator=g)
+        c = torch.empty(m)
+        return timed(lambda: torch.add(a, b, out=c), seconds, 3 * m * 4, 1e9, f"vector add [{m}]")
 
 
 def generic_fma_program(T, n, block=1024):
@@ -321,39 +452,47 @@ class GenericFmaOp(RowOp):
     """A program outside the recognised families: CUDA C generated per program, NVRTC-compiled."""
 
     name = "pointwise"
-    n = 16 * 1024 * 1024
+    full_rows, cols = 16 * 1024 * 1024, 1
     config = "generic elementwise D = A*B + C (separately rounded), A,B,C f32 [16777216] ~N(0,1), NVRTC path"
 
-    def setup(self):
+    def units_of_rows(self, rows):
+        return 4 * rows * 4
+
+    def make_kernel(self, local):
         import ntilang_b200
         from ntilang_b200 import language as T
 
-        self.kernel = ntilang_b200.compile(generic_fma_program(T, self.n), out_idx=[-1])
-        assert self.kernel.spec.family == "pointwise"
-        k = self.sets_needed(4 * self.n * 4)
-        self.sets = []
-        for s in range(k):
-            a, b, c = (self.gen((self.n,), 1.0, 1000 * self.rank + 3 * s + j) for j in range(3))
-            d = self.torch.empty_like(a)
-            self.sets.append(((a, b, c, d), (a, b, c), d))
+        kern = ntilang_b200.compile(generic_fma_program(T, self.rows if local else self.full_rows), out_idx=[-1])
+        assert kern.spec.family == "pointwise"
+        return kern
 
-    def units(self):
-        return 4 * self.n * 4
+    def global_inputs(self):
+        return tuple(self.gen((self.full_rows,), 1.0, j) for j in range(3))
+
+    def slice_inputs(self, full):
+        return tuple(self.take(t) for t in full)
+
+    def local_inputs(self, s):
+        return tuple(self.gen((self.rows,), 1.0, 1000 * self.rank + 3 * s + j) for j in range(3))
 
     def cpu(self, seconds):
         import numpy as np
 
-        m = 4 * 1024 * 1024
+        m = self.full_rows
         a, b, c = (np.random.default_rng(j).normal(size=m).astype(np.float32) for j in range(3))
-        n, t0 = 0, time.perf_counter()
-        while time.perf_counter() - t0 < seconds:
-            np.add(np.multiply(a, b), c)
-            n += 1
-        dt = time.perf_counter() - t0
-        return n * 4 * m * 4 / dt / 1e9, f"{n} x numpy a*b+c [{m}] (float32, separately rounded)"
+        return timed(lambda: np.add(np.multiply(a, b), c), seconds, 4 * m * 4, 1e9,
+                     f"numpy a*b+c [{m}] (float32, separately rounded)")
+
+    def cpu_torch(self, torch, seconds):
+        m = self.full_rows
+        g = torch.Generator().manual_seed(0)
+        a, b, c = (torch.randn(m, generator=g) for _ in range(3))
+        return timed(lambda: a * b + c, seconds, 4 * m * 4, 1e9, f"a*b+c [{m}]")
 
 
-class GemmOp(Op):
+class GemmOp(RowOp):
+    """C = A @ B; a rank computes an M-panel of C from its rows of A and the whole of B."""
+
     name = "gemm"
     bound = "tensor"
     unit = "TFLOP/s"
@@ -362,46 +501,69 @@ class GemmOp(Op):
     epilogue = False
     config = "FP16 GEMM 4096x4096x4096, A,B ~N(0,1)/sqrt(K), C f32"
 
-    def setup(self):
+    def localize(self):
+        self.full_rows = self.m
+        super().localize()
+
+    def units_of_rows(self, rows):
+        return 2 * rows * self.n * self.k
+
+    def make_kernel(self, local):
         from ntilang_b200 import kernels as K
 
-        torch = self.torch
-        self.kernel = (K.matmul_bias_relu if self.epilogue else K.matmul)(self.m, self.n, self.k)
-        foot = (self.m * self.k + self.k * self.n) * 2 + self.m * self.n * 4
-        self.sets = []
-        for s in range(self.sets_needed(foot)):
-            g = torch.Generator(device=self.device).manual_seed(1000 * self.rank + s)
-            a = (torch.randn(self.m, self.k, device=self.device, generator=g) / math.sqrt(self.k)).half()
-            b = (torch.randn(self.k, self.n, device=self.device, generator=g) / math.sqrt(self.k)).half()
-            c = torch.empty(self.m, self.n, device=self.device)
-            if self.epilogue:
-                bias = torch.randn(self.n, device=self.device, generator=g) * 0.1
-                self.sets.append(((a, b, bias, c), (a, b, bias), c))
-            else:
-                self.sets.append(((a, b, c), (a, b), c))
+        return (K.matmul_bias_relu if self.epilogue else K.matmul)(self.rows if local else self.m, self.n, self.k)
 
-    def units(self):
-        return 2 * self.m * self.n * self.k
+    def _ab(self, rows, seed):
+        torch = self.torch
+        g = self.g(seed)
+        a = (torch.randn(rows, self.k, device=self.device, generator=g) / math.sqrt(self.k)).half()
+        b = (torch.randn(self.k, self.n, device=self.device, generator=g) / math.sqrt(self.k)).half()
+        if not self.epilogue:
+            return a, b
+        return a, b, torch.randn(self.n, device=self.device, generator=g) * 0.1
+
+    def global_inputs(self):
+        return self._ab(self.m, 0)
+
+    def slice_inputs(self, full):
+        return (self.take(full[0]),) + tuple(full[1:])
+
+    def local_inputs(self, s):
+        return self._ab(self.rows, 1000 * self.rank + s)
+
+    def out_bytes(self, ins):
+        return ins[0].shape[0] * self.n * 4
+
+    def alloc_out(self, ins):
+        return self.torch.empty(ins[0].shape[0], self.n, device=self.device)
 
     def cpu(self, seconds):
         import numpy as np
 
         from oracle import ntl_oracle as O
 
-        rows = 256
+        rows = self.full_rows
         rng = np.random.default_rng(0)
         a = (rng.normal(size=(rows, self.k)) / 64).astype(np.float16)
         b = (rng.normal(size=(self.k, self.n)) / 64).astype(np.float16)
         bias = rng.normal(0, 0.1, self.n).astype(np.float32)
-        n, t0 = 0, time.perf_counter()
-        while time.perf_counter() - t0 < seconds:
-            if self.epilogue:
-                O.gemm(a, b, bias, O.BIAS_N, relu=True, accumulate=np.float32)
-            else:
-                O.gemm(a, b, accumulate=np.float32)
-            n += 1
-        dt = time.perf_counter() - t0
-        return n * 2 * rows * self.n * self.k / dt / 1e12, f"{n} x fp32 matmul [{rows},{self.k}]x[{self.k},{self.n}]"
+        if self.epilogue:
+            fn = lambda: O.gemm(a, b, bias, O.BIAS_N, relu=True, accumulate=np.float32)  # noqa: E731
+        else:
+            fn = lambda: O.gemm(a, b, accumulate=np.float32)  # noqa: E731
+        return timed(fn, seconds, 2 * rows * self.n * self.k, 1e12, f"fp32 matmul [{rows},{self.k}]x[{self.k},{self.n}]")
+
+    def cpu_torch(self, torch, seconds):
+        rows = self.full_rows
+        g = torch.Generator().manual_seed(0)
+        a = (torch.randn(rows, self.k, generator=g) / 64).half()
+        b = (torch.randn(self.k, self.n, generator=g) / 64).half()
+        bias = torch.randn(self.n, generator=g) * 0.1
+        if self.epilogue:
+            fn = lambda: torch.relu(a.float() @ b.float() + bias)  # noqa: E731
+        else:
+            fn = lambda: a.float() @ b.float()  # noqa: E731
+        return timed(fn, seconds, 2 * rows * self.n * self.k, 1e12, f"fp32 matmul [{rows},{self.k}]x[{self.k},{self.n}]")
 
 
 class GemmBiasReluOp(GemmOp):
@@ -410,7 +572,10 @@ class GemmBiasReluOp(GemmOp):
     config = "FP16 GEMM 4096^3 + fused C=relu(A@B+bias[N]), bias ~N(0,0.1)"
 
 
-class FA2Op(Op):
+class FA2Op(RowOp):
+    """Attention over [B, H, S, D]; a rank takes a contiguous block of the batch (N | B), else of
+    the flattened (batch, head) pairs."""
+
     name = "fa2"
     bound = "tensor"
     unit = "TFLOP/s"
@@ -419,20 +584,47 @@ class FA2Op(Op):
     causal = False
     config = "FlashAttention-2 fwd Q,K,V f16 [8,32,4096,128] ~N(0,1), scale 1/sqrt(128), non-causal"
 
-    def setup(self):
+    def localize(self):
+        self.by_batch = self.B % max(1, self.world) == 0
+        self.full_rows = self.B if self.by_batch else self.B * self.H
+        super().localize()
+
+    def local_shape(self, rows=None):
+        rows = self.rows if rows is None else rows
+        return (rows, self.H, self.S, self.D) if self.by_batch else (rows, 1, self.S, self.D)
+
+    def units_of_rows(self, rows):
+        f = 4 * rows * (self.H if self.by_batch else 1) * self.S * self.S * self.D
+        return f // 2 if self.causal else f
+
+    def make_kernel(self, local):
         from ntilang_b200 import kernels as K
 
-        torch = self.torch
-        self.kernel = K.flash_attention(self.B, self.H, self.S, self.D, self.causal)
-        g = torch.Generator(device=self.device).manual_seed(1000 * self.rank)
-        shape = (self.B, self.H, self.S, self.D)
-        q, k, v = (torch.randn(shape, device=self.device, generator=g).half() for _ in range(3))
-        o = torch.empty_like(q)
-        self.sets = [((q, k, v, o), (q, k, v), o)]
+        if not local:
+            return K.flash_attention(self.B, self.H, self.S, self.D, self.causal)
+        b, h = self.local_shape()[:2]
+        return K.flash_attention(b, h, self.S, self.D, self.causal)
 
-    def units(self):
-        f = 4 * self.B * self.H * self.S * self.S * self.D
-        return f // 2 if self.causal else f
+    def _qkv(self, shape, seed):
+        g = self.g(seed)
+        return tuple(self.torch.randn(shape, device=self.device, generator=g).half() for _ in range(3))
+
+    def global_inputs(self):
+        return self._qkv((self.B, self.H, self.S, self.D), 0)
+
+    def slice_inputs(self, full):
+        if self.by_batch:
+            return tuple(self.take(t) for t in full)
+        return tuple(self.take(t.reshape(self.B * self.H, 1, self.S, self.D)) for t in full)
+
+    def local_inputs(self, s):
+        return self._qkv(self.local_shape(), 1000 * self.rank + s)
+
+    def out_bytes(self, ins):
+        return ins[0].numel() * 2
+
+    def ungather(self, g):
+        return g.reshape(self.B, self.H, self.S, self.D)
 
     def cpu(self, seconds):
         import numpy as np
@@ -444,21 +636,18 @@ class FA2Op(Op):
         q = rng.normal(size=(1, 1, rows, self.D)).astype(np.float16)
         k, v = (rng.normal(size=(1, 1, self.S, self.D)).astype(np.float16) for _ in range(2))
         c = math.log2(math.e) / math.sqrt(self.D)
-        n, t0 = 0, time.perf_counter()
-        flops = 0
-        while time.perf_counter() - t0 < seconds:
-            if self.causal:
-                # the last `rows` queries of a causal head attend to (almost) all keys
-                qq = np.zeros((1, 1, self.S, self.D), np.float16)
-                qq[0, 0, -rows:] = q[0, 0]
-                O.fa2_blockwise(qq[:, :, -rows:], k, v, c, False)
-                flops += 4 * rows * self.S * self.D
-            else:
-                O.fa2_blockwise(q, k, v, c, False)
-                flops += 4 * rows * self.S * self.D
-            n += 1
-        dt = time.perf_counter() - t0
-        return flops / dt / 1e12, f"{n} x attention [1,1,{rows} queries,{self.S} keys,{self.D}]"
+        # causal: the last `rows` queries of a head attend to (almost) all keys, the same work
+        return timed(lambda: O.fa2_blockwise(q, k, v, c, False), seconds, 4 * rows * self.S * self.D, 1e12,
+                     f"attention [1,1,{rows} queries,{self.S} keys,{self.D}]")
+
+    def cpu_torch(self, torch, seconds):
+        rows = 256
+        g = torch.Generator().manual_seed(0)
+        q = torch.randn(1, 1, rows, self.D, generator=g).half().float()
+        k, v = (torch.randn(1, 1, self.S, self.D, generator=g).half().float() for _ in range(2))
+        fn = lambda: torch.nn.functional.scaled_dot_product_attention(q, k, v)  # noqa: E731
+        return timed(fn, seconds, 4 * rows * self.S * self.D, 1e12,
+                     f"fp32 SDPA [1,1,{rows} queries,{self.S} keys,{self.D}]")
 
 
 class FA2CausalOp(FA2Op):
@@ -469,6 +658,18 @@ class FA2CausalOp(FA2Op):
 
 OPS = {c.name: c for c in (CumsumOp, RMSNormOp, SoftmaxOp, VaddOp, GemmOp, GemmBiasReluOp, FA2Op, FA2CausalOp,
                            LayerNormOp, TransposeOp, GenericFmaOp)}
+
+
+def timed(fn, seconds, units_per_call, per_unit, what):
+    """Repeat ``fn`` for about ``seconds``; (throughput, sample description)."""
+    n, t0 = 0, time.perf_counter()
+    while True:
+        fn()
+        n += 1
+        dt = time.perf_counter() - t0
+        if dt >= seconds:
+            break
+    return n * units_per_call / dt / per_unit, f"{n} x {what}"
 
 
 # ------------------------------------------------------------------------------ clocks
@@ -534,18 +735,37 @@ class ClockSampler:
 # ----------------------------------------------------------------------------- measure
 
 
-def run_op(op, torch, dist, world, steps, warmup, stream, peaks, peak_kind, traffic, want_e2e, want_call_path=True):
+class Timer:
+    """Device time of work on ``stream`` between a barrier and a synchronize, max over ranks."""
+
+    def __init__(self, torch, dist, device):
+        self.torch, self.dist, self.device = torch, dist, device
+
+    def max_over_ranks(self, ms):
+        if self.dist is None:
+            return ms
+        t = self.torch.tensor([ms], device=self.device)
+        self.dist.all_reduce(t, op=self.dist.ReduceOp.MAX)
+        return float(t.item())
+
+
+def flush_l2(torch, device, scratch={}):  # noqa: B006 - one scratch buffer per device and process
+    """Evict L2 before a timed region by reading a buffer of twice its size.  Reading (not
+    writing) leaves the cache holding clean lines, so the timed launches pay no write-back of
+    the flush itself."""
+    buf = scratch.get(device)
+    if buf is None:
+        buf = scratch[device] = torch.ones(2 * L2_BYTES // 4, dtype=torch.float32, device=device)
+    return buf.amax()
+
+
+def time_graph(op, torch, dist, steps, stream, timer):
+    """K launches (rotating input sets) captured into one CUDA graph; one untimed replay, an
+    L2 flush, then the timed replay between CUDA events.  Returns (ms per step, launches)."""
     from ntilang_b200 import _lib
 
-    op.setup()
     kern = op.kernel
     nsets = len(op.sets)
-    # warm-up through the public call
-    with torch.cuda.stream(stream):
-        for i in range(max(3, warmup)):
-            kern(*op.sets[i % nsets][0])
-    stream.synchronize()
-    # capture K steps (rotating input sets) into one graph
     before = _lib.launch_count()
     graph = torch.cuda.CUDAGraph()
     with torch.cuda.graph(graph, stream=stream):
@@ -556,6 +776,7 @@ def run_op(op, torch, dist, world, steps, warmup, stream, peaks, peak_kind, traf
     end = torch.cuda.Event(enable_timing=True)
     with torch.cuda.stream(stream):  # replay() launches on the current stream
         graph.replay()  # untimed replay
+        flush_l2(torch, op.device)
         stream.synchronize()
         if dist is not None:
             dist.barrier()
@@ -566,15 +787,26 @@ def run_op(op, torch, dist, world, steps, warmup, stream, peaks, peak_kind, traf
     torch.cuda.synchronize()
     if dist is not None:
         dist.barrier()
-    ms = start.elapsed_time(end)
-    if dist is not None:
-        t = torch.tensor([ms], device=op.device)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
+    ms = timer.max_over_ranks(start.elapsed_time(end))
     del graph
-    ms_step = ms / steps
+    return ms / steps, launches
+
+
+def warm(op, torch, stream, warmup):
+    kern = op.kernel
+    with torch.cuda.stream(stream):
+        for i in range(max(3, warmup)):
+            kern(*op.sets[i % len(op.sets)][0])
+    stream.synchronize()
+
+
+def run_op(op, torch, dist, steps, warmup, stream, peaks, peak_kind, traffic, timer, want_e2e, want_call_path=True):
+    op.setup()
+    warm(op, torch, stream, warmup)
+    ms_step, launches = time_graph(op, torch, dist, steps, stream, timer)
     units = op.units()
-    value = world * units / (ms_step / 1e3) / op.per_unit()
+    total = op.total_units()
+    value = total / (ms_step / 1e3) / op.per_unit()
     per_launch = units / (ms_step / 1e3) / op.per_unit()
     if op.bound == "hbm":
         peak = float(peaks.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"]))
@@ -583,23 +815,51 @@ def run_op(op, torch, dist, world, steps, warmup, stream, peaks, peak_kind, traf
         peak = float(peaks.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"]))
         punit = "TFLOP/s"
     tr = traffic.get(op.name)
+    tr_bytes = None
+    if isinstance(tr, dict) and tr.get("bytes_per_launch") is not None:
+        # the captured launch covers the full single-GPU job; a shard moves its share of it
+        tr_bytes = int(round(tr["bytes_per_launch"] * units / op.whole_job_units()))
     result = {
         "metric": f"{op.name} achieved {op.unit}", "value": round(value, 3), "unit": op.unit,
-        "ms_per_step": round(ms_step, 6), "steps": steps, "buffer_sets": nsets, "gpu_launches": launches,
-        "config": op.config, "dtype": op.dtype,
+        "ms_per_step": round(ms_step, 6), "steps": steps, "buffer_sets": len(op.sets), "gpu_launches": launches,
+        "config": op.config, "dtype": op.dtype, "shard": shard_desc(op),
         "roofline": {"bound": op.bound, "achieved": round(per_launch, 3), "peak": peak, "unit": punit,
-                     "frac": round(per_launch / peak, 4), "peak_source": f"{peak_kind} (MEASURED_PEAKS.json burst)"
-                     if peak_kind == "measured" else "fallback",
-                     "traffic": tr.get("bytes_per_launch") if isinstance(tr, dict) else None,
-                     "algorithmic_per_launch": units},
+                     "frac": round(per_launch / peak, 4),
+                     "peak_source": "measured, burst" if peak_kind == "measured" else "fallback",
+                     "traffic": tr_bytes, "algorithmic_per_launch": units},
     }
     if want_call_path:
         result["python_call"] = measure_call_path(op, torch, stream)
     if want_e2e:
-        result["e2e"] = measure_e2e(op, torch, dist, world, steps, stream)
-    op.sets = None
-    torch.cuda.empty_cache()
+        result["e2e"] = measure_e2e(op, torch, dist, steps, stream, timer)
     return result
+
+
+def shard_desc(op):
+    if op.world == 1:
+        return "whole job"
+    return f"rank {op.rank}: {op.rows} of {op.full_rows} {'rows' if op.bound == 'hbm' else 'panel rows'}"
+
+
+def verify_shards(op, torch, dist, stream):
+    """All-gather the shards' outputs for input set 0 (one seeded global input) and compare
+    them on rank 0, bit for bit, with the same kernels run on the whole job on one GPU."""
+    from ntilang_b200.dist import gather_rows
+
+    with torch.cuda.stream(stream):
+        y = op.kernel(*op.sets[0][1])
+    stream.synchronize()
+    gathered = gather_rows(op.gather_view(y), op.world)
+    if op.rank != 0:
+        return None
+    whole = op.ungather(gathered)
+    full_in = op.global_inputs()
+    kern = op.make_kernel(local=False)
+    with torch.cuda.stream(stream):
+        ref = kern(*full_in)
+    stream.synchronize()
+    same = bool(torch.equal(whole, ref))
+    return {"bit_identical": same, "max_abs_diff": 0.0 if same else float((whole.float() - ref.float()).abs().max())}
 
 
 def measure_call_path(op, torch, stream, calls=200):
@@ -622,7 +882,7 @@ def measure_call_path(op, torch, stream, calls=200):
     return {"us_per_call": round(1e6 * t_all / n, 2), "host_us_per_call": round(1e6 * t_issue / n, 2), "calls": n}
 
 
-def measure_e2e(op, torch, dist, world, steps, stream):
+def measure_e2e(op, torch, dist, steps, stream, timer):
     """Public-call path with host buffers.  Every step copies its inputs host->device from pinned
     memory, makes the public call (``CompiledKernel.__call__``) and copies its output
     device->host.  Steps alternate between two streams, each with its own device and host
@@ -661,18 +921,14 @@ def measure_e2e(op, torch, dist, world, steps, stream):
     stream.wait_stream(lanes[1])
     end.record(stream)
     torch.cuda.synchronize()
-    ms = start.elapsed_time(end)
-    if dist is not None:
-        t = torch.tensor([ms], device=op.device)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
-    ms_step = ms / n
-    value = world * op.units() / (ms_step / 1e3) / op.per_unit()
+    ms_step = timer.max_over_ranks(start.elapsed_time(end)) / n
+    value = op.total_units() / (ms_step / 1e3) / op.per_unit()
     return {"value": round(value, 3), "unit": op.unit, "h2d_bytes_per_step": bi, "d2h_bytes_per_step": bo,
             "ms_per_step": round(ms_step, 4), "steps": n, "streams": 2}
 
 
-def cpu_baseline(op, seconds):
+def cpu_baselines(op, seconds):
+    """The oracle port (``kind: port``) and torch on all host cores, each a bounded sample."""
     try:
         import oracle.rowops as rowops
 
@@ -681,7 +937,13 @@ def cpu_baseline(op, seconds):
         threads = os.cpu_count() or 1
     value, sample = op.cpu(seconds)
     cores = threads if op.bound == "hbm" else (os.cpu_count() or 1)
-    return {"value": round(value, 4), "unit": op.unit, "cores": cores, "kind": "port", "sample": sample}
+    port = {"value": round(value, 4), "unit": op.unit, "cores": cores, "kind": "port", "sample": sample}
+    import torch
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    tval, tsample = op.cpu_torch(torch, seconds)
+    return port, {"value": round(tval, 4), "unit": op.unit, "cores": torch.get_num_threads(), "sample": tsample,
+                  "torch": torch.__version__}
 
 
 # ------------------------------------------------------------------------------ the reference's kernels on the GPU
@@ -715,12 +977,12 @@ def reference_builders(target):
 
     gemm_tiles = dict(block_m=128, block_n=128, block_k=32, num_stages=3, swizzle_panel=8, target=target)
     return {
-        "cumsum": (lambda op: ex("cumsum")(op.rows, op.cols, target=target), same, None),
-        "rmsnorm": (lambda op: ex("rmsnorm")(op.rows, op.cols, eps=op.eps, target=target), same, None),
-        "layernorm": (lambda op: ex("layernorm")(op.rows, op.cols, eps=op.eps, target=target), same, None),
-        "softmax": (lambda op: ex("softmax")(op.rows, op.cols, target=target), same, None),
-        "vadd": (lambda op: ex("vector_add")(op.n, target=target), same, None),
-        "transpose": (lambda op: ex("transpose")(op.m, op.n, target=target), same, None),
+        "cumsum": (lambda op: ex("cumsum")(op.full_rows, op.cols, target=target), same, None),
+        "rmsnorm": (lambda op: ex("rmsnorm")(op.full_rows, op.cols, eps=op.eps, target=target), same, None),
+        "layernorm": (lambda op: ex("layernorm")(op.full_rows, op.cols, eps=op.eps, target=target), same, None),
+        "softmax": (lambda op: ex("softmax")(op.full_rows, op.cols, target=target), same, None),
+        "vadd": (lambda op: ex("vector_add")(op.full_rows, target=target), same, None),
+        "transpose": (lambda op: ex("transpose")(op.full_rows, op.cols, target=target), same, None),
         "gemm": (lambda op: ex("matmul")(op.m, op.n, op.k, **gemm_tiles), same, None),
         # The example's epilogue is relu(0.5 * acc + Bias[M, N]) (examples/matmul_relu.py:35-38):
         # bias[N] is broadcast to a full [M, N] operand and the result checked against torch.
@@ -730,7 +992,7 @@ def reference_builders(target):
                 None),
         "fa2_causal": (lambda op: ex("flash_attention")(op.B, op.H, op.S, op.D, is_causal=True, target=target),
                        same, None),
-        "pointwise": (lambda op: R.compile(generic_fma_program(RT, op.n), target=target), same, None),
+        "pointwise": (lambda op: R.compile(generic_fma_program(RT, op.full_rows), target=target), same, None),
     }
 
 
@@ -847,10 +1109,13 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=("ours", "reference", "reference-gpu"), default="ours")
     ap.add_argument("--ops", default=",".join(OPS))
-    ap.add_argument("--cpu-seconds", type=float, default=2.0, help="CPU-baseline sample per op (0 = skip)")
+    ap.add_argument("--cpu-seconds", type=float, default=1.5, help="CPU-baseline sample per op and path (0 = skip)")
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer end-to-end leg")
     ap.add_argument("--no-call-path", action="store_true",
                     help="skip the Python call-path timing (200 extra launches per op; for launch lists)")
+    ap.add_argument("--no-weak", action="store_true", help="N > 1: skip the full-job-per-rank (weak) timing")
+    ap.add_argument("--detail", default=os.environ.get("NTL_BENCH_DETAIL", DETAIL_DEFAULT),
+                    help="side file for the full per-op records ({n} = number of GPUs; '' = none)")
     ap.add_argument("--gemm-shape", default=None, help="M,N,K override (profiling a small case)")
     ap.add_argument("--fa2-shape", default=None, help="B,H,S,D override (profiling a small case)")
     args = ap.parse_args()
@@ -878,21 +1143,34 @@ def main():
     return run_ours(args, ops)
 
 
+def write_detail(path_tpl, n, record):
+    if not path_tpl:
+        return None
+    path = Path(path_tpl.format(n=n))
+    if not path.is_absolute():
+        path = ROOT / path
+    try:
+        path.parent.mkdir(parents=True, exist_ok=True)
+        path.write_text(json.dumps(record, indent=1))
+    except OSError:
+        return None
+    return str(path.relative_to(ROOT)) if path.is_relative_to(ROOT) else str(path)
+
+
 def run_reference(args, ops):
     """The reference's CPU path (the oracle port of its algorithm) on the host cores."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return 0
-    import torch  # noqa: F401  (same environment as our arm)
+    import torch
 
-    per = {}
+    per, detail = {}, {}
     head = None
     steps = max(1, args.steps)
     for name in ops:
         op = OPS[name](None, None, 0)
         vals = []
-        warm = max(0, min(args.warmup, 1))
-        for _ in range(warm):
+        for _ in range(max(0, min(args.warmup, 1))):
             op.cpu(0.05)
         seconds = max(0.05, min(args.cpu_seconds, 30.0 / (len(ops) * steps)))
         sample = ""
@@ -901,22 +1179,47 @@ def run_reference(args, ops):
             vals.append(v)
         vals.sort()
         v = vals[len(vals) // 2]
-        cb = {"value": round(v, 4), "unit": op.unit, "cores": os.cpu_count() or 1, "kind": "port", "sample": sample}
-        per[name] = {"value": round(v, 4), "unit": op.unit, "config": op.config, "cpu_baseline": cb}
+        cb = {"value": round(v, 4), "unit": op.unit, "cores": os.cpu_count() or 1, "kind": "port", "sample": sample,
+              "cpu": cpu_model()}
+        per[name] = round(v, 4)
+        detail[name] = {"value": round(v, 4), "unit": op.unit, "config": op.config, "cpu_baseline": cb}
         if name == HEADLINE:
             head = (op, v, cb)
     op, v, cb = head
     line = {
         "impl": "reference", "metric": BASELINE_METRIC, "value": round(v, 4), "unit": op.unit, "n_gpus": args.gpus,
-        "steps": steps, "warmup": args.warmup, "ms_per_step": None, "higher_is_better": True, "scaling": "weak",
+        "steps": steps, "warmup": args.warmup, "ms_per_step": None, "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded, BASELINE.json distributions)",
-        "config": {"workload": op.config, "op": op.name, "path": "CPU oracle port of the reference algorithm"},
+        "config": {"workload": op.config, "op": op.name, "path": "CPU oracle port of the reference algorithm",
+                   "torch": torch.__version__},
         "cpu_baseline": cb, "e2e": {"value": round(v, 4), "unit": op.unit, "h2d_bytes_per_step": 0,
                                     "d2h_bytes_per_step": 0},
         "ops": per,
     }
+    where = write_detail(args.detail.replace("bench_detail", "bench_reference_detail") if args.detail else "",
+                         args.gpus, detail)
+    if where:
+        line["detail"] = where
     print(json.dumps(line), flush=True)
     return 0
+
+
+def compact(r):
+    """The per-op figures the one-line record carries."""
+    if "unavailable" in r:
+        return {"unavailable": r["unavailable"][:80]}
+    out = {"value": r["value"], "frac": r["roofline"]["frac"], "ms_per_step": r["ms_per_step"]}
+    if r.get("e2e"):
+        out["e2e"] = r["e2e"]["value"]
+    if r.get("cpu_baseline"):
+        out["cpu"] = r["cpu_baseline"]["value"]
+    if r.get("cpu_torch"):
+        out["cpu_torch"] = r["cpu_torch"]["value"]
+    if r.get("weak"):
+        out["weak"] = r["weak"]["value"]
+    if r.get("verify"):
+        out["verified"] = r["verify"]["bit_identical"]
+    return out
 
 
 def run_ours(args, ops):
@@ -932,7 +1235,7 @@ def run_ours(args, ops):
         import torch.distributed as tdist
 
         torch.cuda.set_device(local)
-        tdist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+        tdist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                  device_id=torch.device(f"cuda:{local}"))
         dist = tdist
     else:
@@ -944,43 +1247,77 @@ def run_ours(args, ops):
     peaks, peak_kind = load_peaks()
     traffic = load_traffic()
     stream = torch.cuda.Stream(device=device)
+    timer = Timer(torch, dist, device)
     sampler = ClockSampler(torch.cuda.current_device())
     sampler.start()
     results = {}
     for name in ops:
-        op = OPS[name](torch, device, rank)
+        op = OPS[name](torch, device, rank, world)
         try:
-            results[name] = run_op(op, torch, dist, world, args.steps, args.warmup, stream, peaks, peak_kind, traffic,
-                                   want_e2e=not args.no_e2e, want_call_path=not args.no_call_path)
+            r = run_op(op, torch, dist, args.steps, args.warmup, stream, peaks, peak_kind, traffic, timer,
+                       want_e2e=not args.no_e2e, want_call_path=not args.no_call_path)
+            if world > 1:
+                r["verify"] = verify_shards(op, torch, dist, stream)
+            op.sets = None
+            if world > 1 and not args.no_weak:
+                full = OPS[name](torch, device, rank, 1)
+                full.setup()
+                warm(full, torch, stream, args.warmup)
+                ms_w, launches_w = time_graph(full, torch, dist, args.steps, stream, timer)
+                r["weak"] = {"value": round(world * full.total_units() / (ms_w / 1e3) / full.per_unit(), 3),
+                             "ms_per_step": round(ms_w, 6), "gpu_launches": launches_w,
+                             "what": "the whole job on every rank"}
+                full.sets = None
+            results[name] = r
         except _lib.KernelError as exc:
             if exc.code != 2:
                 raise
             results[name] = {"unavailable": str(exc)}
             op.sets = None
+        torch.cuda.empty_cache()
     clocks = sampler.stop()
     if rank == 0 and world == 1 and args.cpu_seconds > 0:
         for name in ops:
             if "unavailable" not in results[name]:
-                results[name]["cpu_baseline"] = cpu_baseline(OPS[name](None, None, 0), args.cpu_seconds)
+                port, tcpu = cpu_baselines(OPS[name](None, None, 0), args.cpu_seconds)
+                results[name]["cpu_baseline"], results[name]["cpu_torch"] = port, tcpu
     if dist is not None:
         dist.barrier()
         dist.destroy_process_group()
     if rank != 0:
         return 0
     head = results[HEADLINE]
-    total_launches = sum(r.get("gpu_launches", 0) for r in results.values())
+    total_launches = sum(r.get("gpu_launches", 0) + r.get("weak", {}).get("gpu_launches", 0)
+                         for r in results.values())
+    cb = head.get("cpu_baseline")
+    if cb is not None:
+        cb = dict(cb, cpu=cpu_model(), torch_value=head["cpu_torch"]["value"],
+                  torch_cores=head["cpu_torch"]["cores"])
+    roof = {k: head["roofline"][k] for k in ("bound", "achieved", "peak", "unit", "frac", "traffic")}
+    e2e = head.get("e2e")
+    if e2e is not None:
+        e2e = {k: e2e[k] for k in ("value", "unit", "h2d_bytes_per_step", "d2h_bytes_per_step")}
     line = {
         "metric": BASELINE_METRIC, "value": head["value"], "unit": head["unit"], "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": head["ms_per_step"], "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-        "data": "synthetic (seeded, BASELINE.json shapes and distributions)",
-        "config": {"workload": OPS[HEADLINE].config + " (BASELINE.json configs[1])", "op": HEADLINE,
-                   "parallelism": f"row-sharded x{world}, no collective" if world > 1 else "single GPU",
-                   "l2": "inputs rotated over buffer sets larger than L2 between reuses",
-                   "timing": "K launches replayed from one CUDA graph, CUDA events, max over ranks"},
-        "roofline": head["roofline"], "e2e": head.get("e2e"), "gpu_launches": total_launches, "clocks": clocks,
-        "cpu_baseline": head.get("cpu_baseline"), "ops": results,
+        "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic, seeded, BASELINE shapes",
+        "config": {"workload": OPS[HEADLINE].config + " (configs[1])", "op": HEADLINE,
+                   "parallelism": f"rows split over {world} GPUs, no collective" if world > 1 else "single GPU",
+                   "l2": "buffer sets > 3x L2 between reuses; L2 flushed before timing",
+                   "timing": "CUDA graph of K launches, CUDA events, max over ranks"},
+        "roofline": roof, "e2e": e2e, "gpu_launches": total_launches, "clocks": clocks, "cpu_baseline": cb,
     }
+    if world > 1:
+        line["weak"] = {k: head["weak"][k] for k in ("value", "ms_per_step")} if head.get("weak") else None
+        checked = [r["verify"]["bit_identical"] for r in results.values() if r.get("verify")]
+        line["verify"] = {"gathered_ops": len(checked), "bit_identical": sum(checked),
+                          "against": "whole job on one GPU"}
+    line["op_units"] = "GB/s; TFLOP/s for gemm*, fa2*"
+    line["ops"] = {name: compact(r) for name, r in results.items()}
+    where = write_detail(args.detail, world, {"n_gpus": world, "peaks": peak_kind, "cpu": cpu_model(),
+                                              "clocks": clocks, "ops": results})
+    if where:
+        line["detail"] = where
     print(json.dumps(line), flush=True)
     return 0
 
