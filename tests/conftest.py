@@ -26,6 +26,29 @@ def pytest_configure(config):
     config.addinivalue_line("markers", "slow: long-running CPU test")
 
 
+def reference_examples_dir() -> Path:
+    """Where the reference's own ``examples/*.py`` are read from: ``$NTL_REFERENCE_EXAMPLES``, else
+    the reference install beside the bench (``baseline/_ref/examples``, git-ignored; it travels
+    with the repository to the GPU box)."""
+    env = os.environ.get("NTL_REFERENCE_EXAMPLES")
+    return Path(env) if env else ROOT / "baseline" / "_ref" / "examples"
+
+
+def load_reference_example(name: str):
+    """Import the reference's ``examples/<name>.py`` unchanged.  Its ``import ntilang`` resolves to
+    this repository's alias package (the repository root is first on ``sys.path``); skip when the
+    examples are absent."""
+    import importlib.util
+
+    path = reference_examples_dir() / f"{name}.py"
+    if not path.exists():
+        pytest.skip(f"reference example {path} not present")
+    spec = importlib.util.spec_from_file_location(f"_ref_example_{name}", path)
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    return mod
+
+
 def golden(name: str) -> dict:
     with np.load(GOLDEN / f"{name}.npz") as data:
         return {k: data[k] for k in data.files}

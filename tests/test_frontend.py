@@ -3,7 +3,6 @@
 
 from __future__ import annotations
 
-from pathlib import Path
 
 import pytest
 
@@ -14,7 +13,6 @@ from ntilang_b200 import kernels as K
 from ntilang_b200.compat import normalize_out_idx
 from ntilang_b200.ir import CompileError, ScalarParameter, TensorParameter, TensorType
 
-REFERENCE = Path("/root/reference")
 
 
 def test_alias_package_is_the_implementation():
@@ -297,16 +295,9 @@ def test_markers_raise_when_executed():
         T.prim_func(lambda: None)()
 
 
-@pytest.mark.skipif(not (REFERENCE / "examples").exists(), reason="reference checkout not present")
 def test_reference_examples_are_recognised():
     """The reference's own example programs compile unchanged under ``import ntilang``."""
-    import importlib.util
-
-    def load(name):
-        spec = importlib.util.spec_from_file_location(f"_ex_{name}", REFERENCE / "examples" / f"{name}.py")
-        mod = importlib.util.module_from_spec(spec)
-        spec.loader.exec_module(mod)
-        return mod
+    from tests.conftest import load_reference_example as load
 
     expect = {
         ("vector_add", ()): "elementwise", ("cumsum", ()): "cumsum", ("softmax", ()): "softmax",

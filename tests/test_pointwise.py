@@ -40,15 +40,9 @@ needs_nvrtc = pytest.mark.skipif(not _nvrtc_available(), reason="NVRTC or libntl
 
 
 def _example(name):
-    import importlib.util
+    from tests.conftest import load_reference_example
 
-    path = Path("/root/reference/examples") / f"{name}.py"
-    if not path.exists():
-        pytest.skip("reference checkout not present")
-    spec = importlib.util.spec_from_file_location(f"_pw_ex_{name}", path)
-    mod = importlib.util.module_from_spec(spec)
-    spec.loader.exec_module(mod)
-    return mod
+    return load_reference_example(name)
 
 
 # ------------------------------------------------------------------ oracle vs golden
