@@ -126,10 +126,14 @@ int ntl_gemm_f16_f32_ws(const uint16_t* a, const uint16_t* b, float* c, const fl
  * that passes only tensors and a stream, or a runtime with the device allocator switched
  * off): the split-K scratch lives in a 16 MiB file-scope device array that every GPU
  * loading the library holds until exit.  Shapes whose plan needs more scratch than that
- * return NTL_ERR_UNSUPPORTED.  The first call on a device looks up the array's device
- * address (cudaGetSymbolAddress) and should come before any stream capture.  Calls share
- * the array: flags are cleared on the caller's stream before each launch, and calls that
- * overlap on the GPU race.  No counterpart in the reference (its kernels take no scratch). */
+ * return NTL_ERR_UNSUPPORTED; the need is decided as in ntl_gemm_f16_f32_ws, so operands the
+ * TMA path cannot address (A or B not 16-byte aligned, K or N not a multiple of 8) take the
+ * CUDA-core path, use no scratch and are never refused for size.  The first call on a device
+ * (and the first after a cudaDeviceReset there) looks up the array's device address
+ * (cudaGetSymbolAddress) and should come before any stream capture.  Calls share the array:
+ * a call that uses it first enqueues a 4 KB cudaMemsetAsync of the flag words on the
+ * caller's stream, then the kernel; calls that overlap on the GPU race.  No counterpart in
+ * the reference (its kernels take no scratch). */
 int ntl_gemm_f16_f32_noalloc(const uint16_t* a, const uint16_t* b, float* c, const float* bias, int bias_mode,
                              float alpha, int relu, int64_t M, int64_t N, int64_t K, int b_trans,
                              ntl_stream_t stream);

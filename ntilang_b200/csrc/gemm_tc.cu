@@ -1251,27 +1251,68 @@ extern "C" int ntl_gemm_f16_f32_ws(const uint16_t* a, const uint16_t* b, float* 
 // the GPU race on it.  Host code cannot pass the array's name to a kernel (on the host it
 // is a stand-in, not a device address), so the first call on each device looks up its
 // device address with cudaGetSymbolAddress while that device is current; make that first
-// call before any stream capture.  Nothing here allocates.
+// call before any stream capture.  The address is cached per device together with the id of
+// the context it was looked up in; after cudaDeviceReset the primary context (and the
+// module holding the array) is new, so the next call looks the address up again.  The
+// flag clear is one 4 KB cudaMemsetAsync on the caller's stream, enqueued before the
+// kernel (it is not a kernel of this library and is not counted by ntl_launch_count).
+// Nothing here allocates.
 constexpr size_t kNoAllocScratchBytes = size_t(16) << 20;
 static __device__ __align__(256) unsigned char g_gemm_noalloc_scratch[kNoAllocScratchBytes];
 
 namespace {
 std::mutex g_scratch_mu;
-void* g_scratch_ptr[64] = {};
+struct ScratchAddr {
+  unsigned long long ctx_id;
+  void* ptr;
+};
+ScratchAddr g_scratch[64] = {};
+
+typedef CUresult (*CtxGetCurrentFn)(CUcontext*);
+typedef CUresult (*CtxGetIdFn)(CUcontext, unsigned long long*);
+
+// Id of the calling thread's current context (0 when the driver cannot say).
+unsigned long long current_context_id() {
+  static CtxGetCurrentFn get_current = nullptr;
+  static CtxGetIdFn get_id = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &fn, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_current = reinterpret_cast<CtxGetCurrentFn>(fn);
+    fn = nullptr;
+    if (cudaGetDriverEntryPoint("cuCtxGetId", &fn, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_id = reinterpret_cast<CtxGetIdFn>(fn);
+  });
+  CUcontext ctx = nullptr;
+  unsigned long long id = 0;
+  if (get_current == nullptr || get_id == nullptr || get_current(&ctx) != CUDA_SUCCESS || ctx == nullptr) return 0;
+  if (get_id(ctx, &id) != CUDA_SUCCESS) return 0;
+  return id;
+}
 
 int noalloc_scratch(void** out) {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return ntl_fail(NTL_ERR_CUDA, "cudaGetDevice failed");
   if (dev < 0 || dev >= 64) return ntl_fail(NTL_ERR_UNSUPPORTED, "gemm_noalloc: device index %d out of range", dev);
+  // Make the device's primary context current (cudaSetDevice initialises it) so the id and
+  // the symbol address below refer to the context the launch will use.
+  if (cudaSetDevice(dev) != cudaSuccess) return ntl_fail(NTL_ERR_CUDA, "gemm_noalloc: cudaSetDevice failed");
+  const unsigned long long ctx = current_context_id();
   std::lock_guard<std::mutex> lock(g_scratch_mu);
-  if (g_scratch_ptr[dev] == nullptr) {
+  ScratchAddr& slot = g_scratch[dev];
+  if (slot.ptr == nullptr || ctx == 0 || slot.ctx_id != ctx) {
     void* ptr = nullptr;
     cudaError_t e = cudaGetSymbolAddress(&ptr, g_gemm_noalloc_scratch);
     if (e != cudaSuccess || ptr == nullptr)
       return ntl_fail(NTL_ERR_CUDA, "gemm_noalloc: cudaGetSymbolAddress failed: %s", cudaGetErrorString(e));
-    g_scratch_ptr[dev] = ptr;
+    slot.ptr = ptr;
+    slot.ctx_id = ctx;
   }
-  *out = g_scratch_ptr[dev];
+  *out = slot.ptr;
   return NTL_OK;
 }
 }  // namespace
@@ -1280,13 +1321,20 @@ extern "C" int ntl_gemm_f16_f32_noalloc(const uint16_t* a, const uint16_t* b, fl
                                         int bias_mode, float alpha, int relu, int64_t M, int64_t N, int64_t K,
                                         int b_trans, ntl_stream_t stream) {
   uint64_t need = 0;
-  if (int rc = ntl_gemm_workspace_size(M, N, K, b_trans, &need)) return rc;
+  // The same test gemm_launch applies: operands TMA cannot address take the CUDA-core path,
+  // which needs no scratch (and is then neither refused for size nor preceded by a clear).
+  const bool tma_ok = K > 0 && K % 8 == 0 && (b_trans || N % 8 == 0) && ntl_aligned(a, 16) && ntl_aligned(b, 16);
+  if (tma_ok) {
+    if (int rc = ntl_gemm_workspace_size(M, N, K, b_trans, &need)) return rc;
+  }
   NTL_REQUIRE(need <= kNoAllocScratchBytes, NTL_ERR_UNSUPPORTED,
               "gemm_noalloc: this shape needs %llu bytes of scratch, more than the %zu-byte static maximum "
               "(use ntl_gemm_f16_f32_ws with a caller workspace)",
               (unsigned long long)need, kNoAllocScratchBytes);
   void* scratch = nullptr;
-  if (int rc = noalloc_scratch(&scratch)) return rc;
+  if (need > 0) {
+    if (int rc = noalloc_scratch(&scratch)) return rc;
+  }
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (need > 0) {
     // The flag block at the front of the workspace must start at zero.
