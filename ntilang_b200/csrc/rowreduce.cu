@@ -21,33 +21,40 @@
 namespace {
 
 constexpr unsigned kFull = 0xffffffffu;
-// Rows (warps) per block of the warp-per-row kernels, measured per op on B200 at the BASELINE
-// shapes: softmax 16384x512 is fastest with 8, RMSNorm 4096x1024 with 16 (6.4 vs 6.8 us).
+// Rows (warps) per block of the warp-per-row softmax, measured on B200 at 16384 x 512: 4 beat
+// 2, 8 and 16.
 constexpr int kSoftmaxWarpsPerBlock = 4;
-// The RMSNorm warp kernel takes its rows per block (warps per block) at run time.  While a row
-// fits in 8 chunks of 128 columns the block is sized to ~rows / SMs (4..32 rows), so every SM gets
-// the same number of rows in one block: at 4096 rows, 28-row blocks on 147 SMs (+2% against
-// 16-row blocks, two per SM on 108 SMs and one on 40).  Wider rows use 16-row blocks (a
-// 1024-thread block's 64 registers per thread would spill).  LayerNorm measured 13-18% slower
-// this way and keeps fixed 16-row blocks.
+// The RMSNorm warp kernel takes its rows per block (warps per block) at run time, sized so that
+// two blocks per SM hold every row: ceil(rows / (2 * SMs)), clamped to 4..16 (wider rows: 16).
+// At 4096 x 1024 on 148 SMs that is 14 rows: 0.885 of the copy bandwidth against 0.838 with
+// 16-row blocks, whatever the register cap (graph-replayed launches, 6 interleaved repeats).
 __host__ __device__ constexpr int rms_max_threads(int nch) { return nch <= 8 ? 1024 : 512; }
 int rms_warps_per_block(int64_t rows, int64_t nch) {
   if (nch > 8) return 16;
   int sms = 0;
   if (ntl_num_sms(&sms) != NTL_OK || sms <= 0) return 16;
-  const int64_t per_sm = (rows + sms - 1) / sms;
-  return static_cast<int>(per_sm < 4 ? 4 : (per_sm > 32 ? 32 : per_sm));
+  const int64_t per_block = (rows + 2 * sms - 1) / (2 * sms);
+  return static_cast<int>(per_block < 4 ? 4 : (per_block > 16 ? 16 : per_block));
 }
+// LayerNorm: 16 rows per block, two blocks per SM (4096 x 1024: 0.873 of the copy bandwidth against
+// 0.82 with 14 rows and 0.80 with 8; unlike RMSNorm, which is fastest with 14).
 constexpr int kLayernormWarpsPerBlock = 16;
 
-// Row loads: evict-first (STREAM) by default; softmax measured 3% faster with plain cached
-// loads, RMSNorm 4% slower.
+// Row loads: evict-first (STREAM) or default-cached.  The warp-per-row softmax, RMSNorm and
+// LayerNorm kernels use default-cached loads (softmax +3%, RMSNorm and LayerNorm +4-6% together
+// with the plain stores below, in graph-replayed back-to-back launches on B200).
+//
+// VEC (the dispatch guarantees cols % 4 == 0 and 16-byte aligned rows): a 4-column group is
+// wholly inside or outside the row, so one predicate guards the float4 access.  A per-group
+// bounds test with a scalar fallback path measured 14% slower at 4096 x 1024 (RMSNorm 7.0 vs
+// 6.1 us per launch): the fallback branches kept the row's loads from issuing together.
 template <bool VEC, bool STREAM = true>
 __device__ __forceinline__ void load4(const float* __restrict__ row, int64_t col, int64_t cols, float pad,
                                       float (&v)[4]) {
-  if (VEC && col + 3 < cols) {
+  if (VEC) {
+    float4 t = make_float4(pad, pad, pad, pad);
     const float4* p = reinterpret_cast<const float4*>(row + col);
-    float4 t = STREAM ? __ldcs(p) : __ldg(p);
+    if (col < cols) t = STREAM ? __ldcs(p) : __ldg(p);
     v[0] = t.x, v[1] = t.y, v[2] = t.z, v[3] = t.w;
   } else {
 #pragma unroll
@@ -58,8 +65,9 @@ __device__ __forceinline__ void load4(const float* __restrict__ row, int64_t col
 // Weights are read by every row: cached loads.
 template <bool VEC>
 __device__ __forceinline__ void load_w4(const float* __restrict__ w, int64_t col, int64_t cols, float (&v)[4]) {
-  if (VEC && col + 3 < cols) {
-    float4 t = __ldg(reinterpret_cast<const float4*>(w + col));
+  if (VEC) {
+    float4 t = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    if (col < cols) t = __ldg(reinterpret_cast<const float4*>(w + col));
     v[0] = t.x, v[1] = t.y, v[2] = t.z, v[3] = t.w;
   } else {
 #pragma unroll
@@ -67,14 +75,23 @@ __device__ __forceinline__ void load_w4(const float* __restrict__ w, int64_t col
   }
 }
 
-template <bool VEC>
+// Row stores: evict-first (STREAM) or plain write-back.  The warp-per-row softmax, RMSNorm and
+// LayerNorm kernels measured 1-5% faster with plain stores in back-to-back launches: their
+// output stays in L2 and is written back while the following launches read.
+template <bool VEC, bool STREAM = true>
 __device__ __forceinline__ void store4(float* __restrict__ row, int64_t col, int64_t cols, const float (&v)[4]) {
-  if (VEC && col + 3 < cols) {
-    __stcs(reinterpret_cast<float4*>(row + col), make_float4(v[0], v[1], v[2], v[3]));
+  if (VEC) {
+    float4* p = reinterpret_cast<float4*>(row + col);
+    const float4 t = make_float4(v[0], v[1], v[2], v[3]);
+    if (col < cols) {
+      if (STREAM) __stcs(p, t); else *p = t;
+    }
   } else {
 #pragma unroll
     for (int e = 0; e < 4; ++e)
-      if (col + e < cols) __stcs(row + col + e, v[e]);
+      if (col + e < cols) {
+        if (STREAM) __stcs(row + col + e, v[e]); else row[col + e] = v[e];
+      }
   }
 }
 
@@ -140,7 +157,7 @@ __global__ void __launch_bounds__(kSoftmaxWarpsPerBlock * 32) softmax_rows_warp(
   for (int c = 0; c < NCH; ++c) {
 #pragma unroll
     for (int e = 0; e < 4; ++e) v[c][e] = __fdiv_rn(v[c][e], total);
-    store4<VEC>(yr, static_cast<int64_t>(c) * 128 + lane * 4, cols, v[c]);
+    store4<VEC, false>(yr, static_cast<int64_t>(c) * 128 + lane * 4, cols, v[c]);
   }
 }
 
@@ -215,7 +232,7 @@ __global__ void __launch_bounds__(rms_max_threads(NCH)) rmsnorm_rows_warp(const 
   float* yr = y + row * cols;
   float v[NCH][4];
 #pragma unroll
-  for (int c = 0; c < NCH; ++c) load4<VEC>(xr, static_cast<int64_t>(c) * 128 + lane * 4, cols, 0.0f, v[c]);
+  for (int c = 0; c < NCH; ++c) load4<VEC, false>(xr, static_cast<int64_t>(c) * 128 + lane * 4, cols, 0.0f, v[c]);
   float s[NCH];
 #pragma unroll
   for (int c = 0; c < NCH; ++c) {
@@ -233,7 +250,7 @@ __global__ void __launch_bounds__(rms_max_threads(NCH)) rmsnorm_rows_warp(const 
     load_w4<VEC>(w, col, cols, wv);
 #pragma unroll
     for (int e = 0; e < 4; ++e) v[c][e] = __fmul_rn(__fmul_rn(v[c][e], inv), wv[e]);
-    store4<VEC>(yr, col, cols, v[c]);
+    store4<VEC, false>(yr, col, cols, v[c]);
   }
 }
 
@@ -303,7 +320,9 @@ __device__ __forceinline__ void centre(float (&v)[NCH][4], float mean, int64_t c
 // w and b are read by every row of the block: the block stages both in shared memory once
 // (2 * cols floats) after the dependent-launch wait, so the epilogue reads them at shared-
 // memory latency and the compiler does not hold 8 * NCH weight registers across the row.
-// Up to 8 chunks the kernel is held to 64 registers, two 512-thread blocks per SM.
+// Up to 8 chunks the kernel is held to 64 registers (two 512-thread blocks per SM).  Rows are
+// read with default-cached loads and written with plain stores (9% faster at 4096 x 1024 than
+// evict-first hints, together with the predicated vector accesses of load4/store4).
 template <int NCH, bool VEC>
 __global__ void __launch_bounds__(kLayernormWarpsPerBlock * 32, (NCH <= 8 ? 2 : 1))
     layernorm_rows_warp(const float* __restrict__ x, const float* __restrict__ w, const float* __restrict__ b,
@@ -339,10 +358,10 @@ __global__ void __launch_bounds__(kLayernormWarpsPerBlock * 32, (NCH <= 8 ? 2 : 
       const int col = c * 128 + lane * 4;
       if (VEC) {  // n % 4 == 0: a 4-column group is wholly inside or outside the row
         float4 t = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-        if (col < n) t = __ldcs(reinterpret_cast<const float4*>(xr + col));
+        if (col < n) t = __ldg(reinterpret_cast<const float4*>(xr + col));
         v[c][0] = t.x, v[c][1] = t.y, v[c][2] = t.z, v[c][3] = t.w;
       } else {
-        load4<false>(xr, col, cols, 0.0f, v[c]);
+        load4<false, false>(xr, col, cols, 0.0f, v[c]);
       }
     }
   }
@@ -382,8 +401,7 @@ __global__ void __launch_bounds__(kLayernormWarpsPerBlock * 32, (NCH <= 8 ? 2 : 
     }
 #pragma unroll
     for (int e = 0; e < 4; ++e) v[c][e] = __fadd_rn(__fmul_rn(__fmul_rn(v[c][e], rstd), wv[e]), bv[e]);
-    if (VEC) __stcs(reinterpret_cast<float4*>(yr + col), make_float4(v[c][0], v[c][1], v[c][2], v[c][3]));
-    else store4<false>(yr, col, cols, v[c]);
+    store4<VEC, false>(yr, col, cols, v[c]);
   }
 }
 
