@@ -838,6 +838,11 @@ def run_op(op, torch, dist, steps, warmup, stream, peaks, peak_kind, traffic, ti
     return result
 
 
+def whole_job_op(cls, torch, device):
+    """The weak-scaling leg's op on any rank: the whole BASELINE job, as the only rank of one."""
+    return cls(torch, device, 0, 1)
+
+
 def shard_desc(op):
     if op.world == 1:
         return "whole job"
@@ -1265,7 +1270,7 @@ def run_ours(args, ops):
                 r["verify"] = verify_shards(op, torch, dist, stream)
             op.sets = None
             if world > 1 and not args.no_weak:
-                full = OPS[name](torch, device, rank, 1)
+                full = whole_job_op(OPS[name], torch, device)
                 full.setup()
                 warm(full, torch, stream, args.warmup)
                 ms_w, launches_w = time_graph(full, torch, dist, args.steps, stream, timer)

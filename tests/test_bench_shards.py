@@ -74,3 +74,12 @@ def test_rank_work_adds_up_to_the_baseline_job(name, world):
     assert total == whole + extra
     assert max(o.rows for o in ops) - min(o.rows for o in ops) <= 1
     assert math.isclose(sum(o.rows for o in ops), ops[0].full_rows)
+
+
+@pytest.mark.parametrize("name", sorted(bench.OPS))
+def test_weak_leg_runs_the_whole_job_on_every_rank(name):
+    """``--gpus N`` also times a full-size job on each rank: that op is the whole job whatever the
+    rank's index."""
+    whole = bench.whole_job_op(bench.OPS[name], None, None)
+    assert whole.world == 1 and whole.rank == 0 and whole.rows == whole.full_rows
+    assert whole.total_units() == bench.OPS[name](None, None, 0, 1).units()
