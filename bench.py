@@ -676,14 +676,20 @@ def timed(fn, seconds, units_per_call, per_unit, what):
 
 
 class ClockSampler:
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+    """nvidia-smi samples (every 20 ms) of the SM clock, power and throttle reasons during the
+    run: ``stop()`` summarises the whole run, ``window(t0, t1)`` the samples inside one op's
+    timed region (host wall-clock bounds)."""
+
+    FIELDS = ("timestamp,index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    REASONS = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
 
     def __init__(self, gpu_index):
         self.gpu = gpu_index
         self.proc = None
         self.path = None
+        self.rows = []  # (unix time, sm MHz, max MHz, power W, active reasons)
 
     def start(self):
         import tempfile
@@ -692,44 +698,59 @@ class ClockSampler:
         try:
             self.fh = open(self.path, "w")
             self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "50",
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "20",
                  "-i", str(self.gpu)], stdout=self.fh, stderr=subprocess.DEVNULL)
         except (OSError, FileNotFoundError):
             self.proc = None
 
+    @staticmethod
+    def _num(x):
+        try:
+            return float(x)
+        except ValueError:
+            return None
+
     def stop(self):
         if self.proc is None:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        import datetime
+
         self.proc.terminate()
         try:
             self.proc.wait(5)
         except subprocess.TimeoutExpired:
             self.proc.kill()
         self.fh.close()
-        rows = []
         for line in Path(self.path).read_text().splitlines():
             parts = [p.strip() for p in line.split(",")]
-            if len(parts) >= 9:
-                rows.append(parts)
-        os.unlink(self.path)
-        if not rows:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
-
-        def num(x):
+            if len(parts) < 10:
+                continue
             try:
-                return float(x)
+                ts = datetime.datetime.strptime(parts[0], "%Y/%m/%d %H:%M:%S.%f").timestamp()
             except ValueError:
-                return None
-
-        sm = [num(r[1]) for r in rows if num(r[1]) is not None]
-        mx = [num(r[2]) for r in rows if num(r[2]) is not None]
-        power = [num(r[3]) for r in rows if num(r[3]) is not None]
-        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
-        reasons = sorted({n for r in rows for n, v in zip(names, r[5:9]) if v.lower() == "active"})
-        loaded = [s for s, p in zip(sm, power) if p is not None and p > 300] or sm
-        loaded.sort()
+                continue
+            active = tuple(n for n, v in zip(self.REASONS, parts[6:10]) if v.lower() == "active")
+            self.rows.append((ts, self._num(parts[2]), self._num(parts[3]), self._num(parts[4]), active))
+        os.unlink(self.path)
+        if not self.rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        sm = [r[1] for r in self.rows if r[1] is not None]
+        mx = [r[2] for r in self.rows if r[2] is not None]
+        power = [r[3] for r in self.rows if r[3] is not None]
+        reasons = sorted({n for r in self.rows for n in r[4]})
+        loaded = sorted(r[1] for r in self.rows if r[1] is not None and r[3] is not None and r[3] > 300) or sorted(sm)
         return {"sm_mhz": loaded[len(loaded) // 2] if loaded else None, "sm_max_mhz": max(mx) if mx else None,
-                "reasons": reasons, "samples": len(rows), "power_w_max": max(power) if power else None}
+                "reasons": reasons, "samples": len(self.rows), "power_w_max": max(power) if power else None}
+
+    def window(self, t0, t1):
+        """Median SM clock and power of the samples taken in [t0, t1]."""
+        sel = [r for r in self.rows if t0 <= r[0] <= t1 and r[1] is not None]
+        if not sel:
+            return {"samples": 0}
+        sm = sorted(r[1] for r in sel)
+        pw = sorted(r[3] for r in sel if r[3] is not None)
+        return {"sm_mhz": sm[len(sm) // 2], "power_w": pw[len(pw) // 2] if pw else None, "samples": len(sel),
+                "reasons": sorted({n for r in sel for n in r[4]})}
 
 
 # ----------------------------------------------------------------------------- measure
@@ -784,10 +805,12 @@ def time_graph(op, torch, dist, steps, stream, timer):
         # GPU is still busy with it while the host submits the graph: the host's submission
         # latency stays outside the timed region.
         flush_l2(torch, op.device)
+        t0 = time.time()
         start.record(stream)
         graph.replay()
         end.record(stream)
     torch.cuda.synchronize()
+    op.timed_window = (t0, time.time())
     if dist is not None:
         dist.barrier()
     ms = timer.max_over_ranks(start.elapsed_time(end))
@@ -823,6 +846,7 @@ def run_op(op, torch, dist, steps, warmup, stream, peaks, peak_kind, traffic, ti
         # the captured launch covers the full single-GPU job; a shard moves its share of it
         tr_bytes = int(round(tr["bytes_per_launch"] * units / op.whole_job_units()))
     result = {
+        "window": op.timed_window,
         "metric": f"{op.name} achieved {op.unit}", "value": round(value, 3), "unit": op.unit,
         "ms_per_step": round(ms_step, 6), "steps": steps, "buffer_sets": len(op.sets), "gpu_launches": launches,
         "config": op.config, "dtype": op.dtype, "shard": shard_desc(op),
@@ -1286,6 +1310,15 @@ def run_ours(args, ops):
             op.sets = None
         torch.cuda.empty_cache()
     clocks = sampler.stop()
+    for name, r in results.items():
+        if "window" in r:
+            r["clocks"] = sampler.window(*r.pop("window"))
+            if r["roofline"]["bound"] == "tensor":
+                # the tensor kernels run at the power cap inside their timed region: beside the burst
+                # fraction, the fraction of the sustained (seconds-long, power-capped) GEMM rate
+                sus = float(peaks.get("bf16_tflops_sustained", FALLBACK_PEAKS["bf16_tflops_sustained"]))
+                r["roofline"]["peak_sustained"] = sus
+                r["roofline"]["frac_sustained"] = round(r["roofline"]["achieved"] / sus, 4)
     if rank == 0 and world == 1 and args.cpu_seconds > 0:
         for name in ops:
             if "unavailable" not in results[name]:

@@ -109,25 +109,46 @@ def test_fa2_baseline_size_sampled_heads(torch_cuda, causal):
         torch.testing.assert_close(out[b:b + 1, h:h + 1].float(), ref, rtol=0, atol=ATOL)
 
 
-def test_fa2_timeout_path_reports_error(torch_cuda):
+@pytest.mark.parametrize("causal", [False, True])
+def test_fa2_timeout_path_reports_error(torch_cuda, causal):
+    """A 1-poll wait limit makes the bounded waits give up, in the one-CTA-per-unit kernel
+    (non-causal) and the persistent one (causal, several units per CTA): the launch must return,
+    report a status and leave the context usable."""
     torch = torch_cuda
     from ntilang_b200 import _lib
 
-    q, k, v = (torch.randn(1, 2, 512, 128, device="cuda", dtype=torch.float16) for _ in range(3))
+    b, h, s, d = (1, 2, 512, 128) if not causal else (2, 8, 1024, 128)
+    q, k, v = (torch.randn(b, h, s, d, device="cuda", dtype=torch.float16) for _ in range(3))
     o = torch.empty_like(q)
     _lib.clear_device_status()
     _lib.set_wait_limit(1)
     try:
-        _lib.call("ntl_fa2_fwd_f16", q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), 1, 2, 512, 128,
-                  math.log2(math.e) / math.sqrt(128), 0, torch.cuda.current_stream().cuda_stream)
+        _lib.call("ntl_fa2_fwd_f16", q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), b, h, s, d,
+                  math.log2(math.e) / math.sqrt(d), int(causal), torch.cuda.current_stream().cuda_stream)
         torch.cuda.synchronize()
         status = _lib.device_status()
     finally:
         _lib.set_wait_limit(1 << 26)
         _lib.clear_device_status()
     assert status != 0
-    out = K.flash_attention(1, 2, 512, 128)(q, k, v)
-    torch.testing.assert_close(out.float(), sdpa_fp32(torch, q, k, v, False), rtol=0, atol=ATOL)
+    out = K.flash_attention(b, h, s, d, causal)(q, k, v)
+    torch.testing.assert_close(out.float(), sdpa_fp32(torch, q, k, v, causal), rtol=0, atol=ATOL)
+
+
+@pytest.mark.parametrize("b,h,s", [(3, 5, 600), (1, 1, 100), (2, 3, 4096), (64, 16, 512)])
+def test_fa2_causal_persistent_unit_counts(torch_cuda, b, h, s):
+    """Causal attention runs on the persistent grid: an odd number of units (the last pair has one)
+    with a dead second query tile in the last query block (S = 600, 100), fewer pairs of units than
+    SMs, and several pairs per CTA; sampled heads against fp32 attention."""
+    torch = torch_cuda
+    d = 128
+    g = torch.Generator(device="cuda").manual_seed(b * 1000 + h * 10 + s)
+    q, k, v = (torch.randn(b, h, s, d, device="cuda", generator=g, dtype=torch.float16) for _ in range(3))
+    out = K.flash_attention(b, h, s, d, True)(q, k, v)
+    torch.cuda.synchronize()
+    for bb, hh in {(0, 0), (b - 1, h - 1), (b // 2, h // 2)}:
+        ref = sdpa_fp32(torch, q[bb:bb + 1, hh:hh + 1], k[bb:bb + 1, hh:hh + 1], v[bb:bb + 1, hh:hh + 1], True)
+        torch.testing.assert_close(out[bb:bb + 1, hh:hh + 1].float(), ref, rtol=0, atol=ATOL)
 
 
 def test_fa2_rejects_unsupported_head_dim(torch_cuda):
