@@ -141,6 +141,9 @@ int ntl_gemm_f16_f32_noalloc(const uint16_t* a, const uint16_t* b, float* c, con
 /* FlashAttention-2 forward, fp16 Q,K,V,O [batch, heads, seq, dim] row-major.
  *   O = softmax_base2((Q K^T) * scale_log2 [causal: key <= query]) V, with P rounded to fp16
  *   before the P V product and fp32 softmax statistics.
+ * Non-causal launches one CTA per (batch, head, 256-query block); causal launches a persistent
+ * grid of one CTA per SM (fewer for small problems) that runs the blocks in a fixed order, so
+ * kernels on other streams share SMs with it only as its CTAs finish.
  * Replaces the FFI call of the kernel emitted for examples/flash_attention.py:26-79
  * (scale = log2(e)/sqrt(d) at :23, causal fill at :56-62, P cast at :74-75). */
 int ntl_fa2_fwd_f16(const uint16_t* q, const uint16_t* k, const uint16_t* v, uint16_t* o, int64_t batch,
