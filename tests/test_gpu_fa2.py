@@ -110,6 +110,26 @@ def test_fa2_baseline_size_sampled_heads(torch_cuda, causal):
 
 
 @pytest.mark.parametrize("causal", [False, True])
+def test_fa2_baseline_size_every_head(torch_cuda, causal):
+    """BASELINE config [8, 32, 4096, 128]: all 256 (batch, head) outputs within 2e-3 of fp32 attention
+    computed on the GPU, 16 heads at a time."""
+    torch = torch_cuda
+    gen = torch.Generator(device="cuda").manual_seed(1)
+    shape = (8, 32, 4096, 128)
+    q, k, v = (torch.randn(shape, device="cuda", generator=gen, dtype=torch.float16) for _ in range(3))
+    out = K.flash_attention(*shape, causal)(q, k, v)
+    torch.cuda.synchronize()
+    worst = 0.0
+    for b in range(8):
+        for h0 in range(0, 32, 16):
+            sl = (slice(b, b + 1), slice(h0, h0 + 16))
+            ref = sdpa_fp32(torch, q[sl], k[sl], v[sl], causal)
+            worst = max(worst, float((out[sl].float() - ref).abs().max()))
+            del ref
+    assert worst <= ATOL, worst
+
+
+@pytest.mark.parametrize("causal", [False, True])
 def test_fa2_timeout_path_reports_error(torch_cuda, causal):
     """A 1-poll wait limit makes the bounded waits give up, in the one-CTA-per-unit kernel
     (non-causal) and the persistent one (causal, several units per CTA): the launch must return,
