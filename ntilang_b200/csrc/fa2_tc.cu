@@ -110,7 +110,11 @@ __device__ __forceinline__ uint32_t pack_half2(float a, float b) {
 // 2^n added to the exponent bits.  x is clamped at -126 so the exponent never underflows;
 // such terms (masked or tiny scores) become ~1e-38, i.e. 0 in fp16 P.  Used for a fixed
 // quarter of the exponentials so the MUFU ex2 unit and the FMA pipe share the load.
-// Two values per call, with f32x2 arithmetic.
+// Two values per call, with f32x2 arithmetic.  The method is additive range reduction
+// (W. J. Cody and W. Waite, "Software Manual for the Elementary Functions", 1980) with the
+// result's exponent written straight into the float's bits (N. N. Schraudolph, "A Fast,
+// Compact Approximation of the Exponential Function", Neural Computation 11(4), 1999); the
+// cubic's coefficients were fitted for this kernel.
 __device__ __forceinline__ void exp2_fma2(uint64_t x2, float& p0, float& p1) {
   constexpr float kRound = 12582912.0f;
   float x0, x1;

@@ -14,38 +14,70 @@ have no per-program CUDA source).
 
 from __future__ import annotations
 
-from collections.abc import Callable
+from collections.abc import Callable, Mapping
 from dataclasses import dataclass
 from pathlib import Path
+from types import MappingProxyType
 
 from . import frontend
 from .compat import normalize_out_idx, resolve_target
 from .compiler import CompiledKernel, DynamicJitKernel, lower_program, make_kernel
-from .ir import CompileError
+from .ir import CompileError, ScalarParameter, SymDim
 from .language import PrimFunc, has_symbolic_annotations
+
+
+def _dim_text(n) -> str:
+    return n.name if isinstance(n, SymDim) else str(n)
+
+
+def _expr_text(e) -> str:
+    """Infix text of a launch-shape expression (integers, symbolic sizes, + - * // %)."""
+    if isinstance(e, frontend.Const):
+        return str(e.value)
+    if isinstance(e, frontend.Var):
+        return e.name.rsplit(":", 1)[-1]
+    if isinstance(e, frontend.Bin):
+        return f"({_expr_text(e.a)} {e.op} {_expr_text(e.b)})"
+    return str(e)
 
 
 @dataclass(frozen=True)
 class Artifact:
+    """One emitted text (``format`` is ``"python"`` or ``"cuda"``)."""
+
     format: str
     content: str
 
     def save(self, path) -> Path:
-        target = Path(path)
-        target.parent.mkdir(parents=True, exist_ok=True)
-        target.write_text(self.content, encoding="utf-8", newline="\n")
-        return target
+        """Write the text as UTF-8 with ``\\n`` line ends, creating missing folders; returns the path."""
+        out = Path(path)
+        if not out.parent.is_dir():
+            out.parent.mkdir(parents=True)
+        with open(out, "w", encoding="utf-8", newline="\n") as fh:
+            fh.write(self.content)
+        return out
 
 
 @dataclass(frozen=True)
 class Program:
+    """A parsed program and the front end that read it."""
+
     ir: frontend.Program
     frontend: str
     name: str
 
     def as_text(self) -> str:
-        params = ", ".join(p.name for p in self.ir.params)
-        return f"Program(frontend={self.frontend!r}, name={self.name!r}, params=({params}), threads={self.ir.threads})"
+        """A short listing: the program's name, its parameters with types, and its launch shape."""
+        lines = [f"program {self.name} [frontend {self.frontend}]"]
+        for prm in self.ir.params:
+            if isinstance(prm, ScalarParameter):
+                lines.append(f"  {prm.name}: {prm.dtype}")
+            else:
+                dims = ", ".join(_dim_text(n) for n in prm.type.shape)
+                lines.append(f"  {prm.name}: {prm.type.dtype}[{dims}]")
+        grid = ", ".join(_expr_text(g) for g in self.ir.grid)
+        lines.append(f"  launch: grid ({grid}), {self.ir.threads} threads per block")
+        return "\n".join(lines)
 
 
 @dataclass(frozen=True)
@@ -66,7 +98,8 @@ class LoweredProgram:
                 raise CompileError(f"{self.program.name}: runs the prebuilt `{spec.family}` kernel of "
                                    "libntl_kernels.so; there is no per-program CUDA source to emit")
             return Artifact(format=format, content=spec.params["kernel"].source)
-        raise CompileError(f"Unsupported emit format {format!r} for backend {self.backend!r}")
+        raise CompileError(f"Unsupported emit format {format!r}: the {self.backend!r} back end writes 'python' "
+                           "(the launcher module) or 'cuda' (a generated elementwise kernel)")
 
 
 @dataclass(frozen=True)
@@ -75,19 +108,28 @@ class ArtifactBundle:
     kernel: CompiledKernel
 
 
-class RuntimeModule:
-    """Loaded executable container exposing entry points by kernel name."""
+class RuntimeModule(Mapping):
+    """The built kernels of one bundle, looked up by program name (``module["scale"]``).
+
+    A read-only mapping: ``in``, ``len``, iteration over names and ``keys()`` work as for a dict.
+    """
 
     def __init__(self, bundle: ArtifactBundle, device: str = "cuda:0"):
         self.bundle = bundle
         self.device = device
-        self._entries = {bundle.lowered.program.name: bundle.kernel}
+        self._by_name = MappingProxyType({bundle.lowered.program.name: bundle.kernel})
 
     def __getitem__(self, name: str) -> CompiledKernel:
-        return self._entries[name]
+        try:
+            return self._by_name[name]
+        except KeyError:
+            raise KeyError(f"no kernel named {name!r} in this module (it holds {', '.join(self._by_name)})") from None
 
-    def __contains__(self, name: str) -> bool:
-        return name in self._entries
+    def __iter__(self):
+        return iter(self._by_name)
+
+    def __len__(self) -> int:
+        return len(self._by_name)
 
 
 def _sm100a_backend(ir: frontend.Program, target: str, out_idx) -> CompiledKernel:
@@ -109,18 +151,22 @@ class Compiler:
         """``emitter_fn(ir, target, out_idx) -> CompiledKernel``."""
         self._backends[name] = emitter_fn
 
+    @staticmethod
+    def _lookup(table: dict, kind: str, name: str) -> Callable:
+        fn = table.get(name)
+        if fn is None:
+            raise CompileError(f"Unknown {kind} {name!r}: this Compiler knows {sorted(table)}")
+        return fn
+
     def import_program(self, source, *, frontend: str = "tilelang") -> Program:
-        if frontend not in self._frontends:
-            raise CompileError(f"Unknown frontend {frontend!r}; registered: {', '.join(sorted(self._frontends))}")
-        ir = self._frontends[frontend](source)
+        ir = self._lookup(self._frontends, "frontend", frontend)(source)
         return Program(ir=ir, frontend=frontend, name=ir.name)
 
     def lower(self, program: Program, *, backend: str = "sm100a", target: str = "auto", out_idx=None) -> LoweredProgram:
-        if backend not in self._backends:
-            raise CompileError(f"Unknown backend {backend!r}; registered: {', '.join(sorted(self._backends))}")
+        emit = self._lookup(self._backends, "backend", backend)
         resolved = resolve_target(target)
         normalized = normalize_out_idx(out_idx, program.ir.params)
-        kernel = self._backends[backend](program.ir, resolved, normalized)
+        kernel = emit(program.ir, resolved, normalized)
         return LoweredProgram(program=program, backend=backend, target=resolved, source=kernel.source,
                               out_idx=normalized, kernel=kernel)
 

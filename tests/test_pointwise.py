@@ -283,6 +283,38 @@ def test_saved_module_compiles_without_ntilang(tmp_path):
         assert out.returncode == 0 and out.stdout.strip() == "ok", out.stderr
 
 
+def test_program_listing_and_runtime_module_lookup():
+    """``Program.as_text`` lists parameters with types and the launch shape (symbolic sizes by
+    name); ``RuntimeModule`` is a read-only mapping from program name to kernel."""
+    from ntilang_b200.pipeline import RuntimeModule
+
+    M = T.dynamic("m")
+
+    @T.prim_func
+    def rows(A: T.Tensor((M, 128), "float32"), B: T.Tensor((M, 128), "float32"), alpha: T.float32):
+        with T.Kernel(T.ceildiv(M, 4), threads=128) as bx:
+            for i, j in T.Parallel(4, 128):
+                B[bx * 4 + i, j] = A[bx * 4 + i, j] * alpha
+
+    compiler = ntilang.Compiler()
+    text = compiler.import_program(rows).as_text().splitlines()
+    assert text == ["program rows [frontend tilelang]", "  A: float32[m, 128]", "  B: float32[m, 128]",
+                    "  alpha: float32", "  launch: grid (((m + 3) // 4)), 128 threads per block"]
+
+    @T.prim_func
+    def scale(A: T.Tensor((64,), "float32"), B: T.Tensor((64,), "float32")):
+        with T.Kernel(1, threads=64):
+            for i in T.Parallel(64):
+                B[i] = A[i] * 2.0
+
+    bundle = compiler.compile(compiler.lower(compiler.import_program(scale), out_idx=[-1]))
+    module = RuntimeModule(bundle)
+    assert list(module) == ["scale"] and len(module) == 1 and "scale" in module
+    assert module["scale"] is bundle.kernel and module.get("other") is None
+    with pytest.raises(KeyError, match="no kernel named 'other'"):
+        module["other"]
+
+
 def test_staged_compiler_api_and_artifact_save(tmp_path):
     """The reference's tests/test_m34_features.py:53-68 under import ntilang."""
 
