@@ -1329,6 +1329,16 @@ def run_ours(args, ops):
         dist.destroy_process_group()
     if rank != 0:
         return 0
+    where = write_detail(args.detail, world, {"n_gpus": world, "peaks": peak_kind, "cpu": cpu_model(),
+                                              "clocks": clocks, "ops": results})
+    print(json.dumps(assemble_line(args.steps, args.warmup, world, results, clocks, where)), flush=True)
+    return 0
+
+
+def assemble_line(steps, warmup, world, results, clocks, detail_path):
+    """The one JSON record rank 0 prints: the headline op's figures at the top level, every op's
+    compact figures under ``ops``.  It must fit the last ~3,000 characters of stdout that the
+    driver keeps (``tests/test_bench_shards.py`` checks the worst case)."""
     head = results[HEADLINE]
     total_launches = sum(r.get("gpu_launches", 0) + r.get("weak", {}).get("gpu_launches", 0)
                          for r in results.values())
@@ -1342,7 +1352,7 @@ def run_ours(args, ops):
         e2e = {k: e2e[k] for k in ("value", "unit", "h2d_bytes_per_step", "d2h_bytes_per_step")}
     line = {
         "metric": BASELINE_METRIC, "value": head["value"], "unit": head["unit"], "n_gpus": world,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": head["ms_per_step"], "higher_is_better": True,
+        "steps": steps, "warmup": warmup, "ms_per_step": head["ms_per_step"], "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic, seeded, BASELINE shapes",
         "config": {"workload": OPS[HEADLINE].config + " (configs[1])", "op": HEADLINE,
                    "parallelism": f"rows split over {world} GPUs, no collective" if world > 1 else "single GPU",
@@ -1357,12 +1367,9 @@ def run_ours(args, ops):
                           "against": "whole job on one GPU"}
     line["op_units"] = "GB/s; TFLOP/s for gemm*, fa2*"
     line["ops"] = {name: compact(r) for name, r in results.items()}
-    where = write_detail(args.detail, world, {"n_gpus": world, "peaks": peak_kind, "cpu": cpu_model(),
-                                              "clocks": clocks, "ops": results})
-    if where:
-        line["detail"] = where
-    print(json.dumps(line), flush=True)
-    return 0
+    if detail_path:
+        line["detail"] = detail_path
+    return line
 
 
 if __name__ == "__main__":

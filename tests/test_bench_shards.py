@@ -83,3 +83,31 @@ def test_weak_leg_runs_the_whole_job_on_every_rank(name):
     whole = bench.whole_job_op(bench.OPS[name], None, None)
     assert whole.world == 1 and whole.rank == 0 and whole.rows == whole.full_rows
     assert whole.total_units() == bench.OPS[name](None, None, 0, 1).units()
+
+
+@pytest.mark.parametrize("world", [1, 8])
+def test_the_json_line_fits_the_driver_tail(world, monkeypatch):
+    """The driver keeps the last ~3,000 characters of the bench's stdout: the one-line record, with
+    every op's figures at their longest, stays under 2,900."""
+    monkeypatch.setattr(bench, "cpu_model", lambda: "Intel(R) Xeon(R) Platinum 8480C Processor @ 2.00GHz x")
+    results = {}
+    for name in bench.OPS:
+        r = {"value": 12345.678, "unit": "GB/s", "ms_per_step": 1.922682, "gpu_launches": 50,
+             "roofline": {"bound": "hbm", "achieved": 12345.678, "peak": 6455.6, "unit": "GB/s", "frac": 1.0686,
+                          "traffic": 165965158},
+             "e2e": {"value": 141.485, "unit": "GB/s", "h2d_bytes_per_step": 201326592,
+                     "d2h_bytes_per_step": 67108864}}
+        if world == 1:
+            r["cpu_baseline"] = {"value": 434.6357, "unit": "GB/s", "cores": 224, "kind": "port",
+                                 "sample": "6480 x cumsum [32768,256]"}
+            r["cpu_torch"] = {"value": 434.6357, "cores": 224}
+        else:
+            r["weak"] = {"value": 98765.432, "ms_per_step": 1.922682, "gpu_launches": 50}
+            r["verify"] = {"bit_identical": True}
+        results[name] = r
+    clocks = {"sm_mhz": 1965.0, "sm_max_mhz": 1965.0, "reasons": ["sw_power_cap", "sw_thermal_slowdown"],
+              "samples": 1335, "power_w_max": 1000.61}
+    line = bench.assemble_line(50, 5, world, results, clocks, f"gpurun_out/bench_detail_n{world}.json")
+    text = bench.json.dumps(line)
+    assert len(text) <= 2900, len(text)
+    assert set(line["ops"]) == set(bench.OPS) and line["n_gpus"] == world and line["value"] == 12345.678
