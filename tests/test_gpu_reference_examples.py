@@ -3,13 +3,15 @@
 Each hot-path ``examples/*.py`` of the reference (``vector_add.py:5-10``, ``cumsum.py:7-14``,
 ``scan.py:7-22``, ``softmax.py:9-25``, ``rmsnorm.py:13-37``, ``layernorm.py:9-45``,
 ``transpose.py:5-15``, ``matmul.py:17-31``, ``matmul_relu.py:17-38``,
-``flash_attention.py:26-79``) is imported from the reference's tree (``tests.conftest.
+``flash_attention.py:26-79``), and the generic elementwise programs ``piecewise.py``,
+``fragment_affine.py`` and ``window_sum.py``, is imported from the reference's tree (``tests.conftest.
 reference_examples_dir``) with ``import ntilang`` resolving to this repository, built with its
 own function at the BASELINE shapes for ``target="auto"`` and launched on the B200.  The outputs
 are checked at the north-star bars: bit-exact (vector add, scans, transpose), 1e-5 relative
 (softmax, RMSNorm, LayerNorm), 1e-3 * (|ref| + max |ref|) of an fp32 product (GEMMs, the
 example's ``relu(0.5 * acc + Bias[M, N])`` epilogue for matmul_relu), 2e-3 absolute against fp32
-attention on sampled heads."""
+attention on sampled heads; the generic programs bit-exact against the outputs the reference's
+own evaluator gave for the same inputs (``tests/golden/pw_*.npz``)."""
 
 from __future__ import annotations
 
@@ -17,7 +19,7 @@ import numpy as np
 import pytest
 
 from oracle import ntl_oracle as O
-from tests.conftest import load_reference_example
+from tests.conftest import golden, load_reference_example
 from tests.test_gpu_fa2 import ATOL, sdpa_fp32
 
 pytestmark = pytest.mark.gpu
@@ -160,3 +162,28 @@ def test_flash_attention_example(torch_cuda, causal):
     for b, h in ((0, 0), (2, 17), (7, 31)):
         ref = sdpa_fp32(torch, q[b:b + 1, h:h + 1], k[b:b + 1, h:h + 1], v[b:b + 1, h:h + 1], causal)
         torch.testing.assert_close(o[b:b + 1, h:h + 1].float(), ref, rtol=0, atol=ATOL)
+
+
+def test_generic_elementwise_examples(torch_cuda):
+    """examples/piecewise.py, fragment_affine.py and window_sum.py at their default sizes, through
+    the NVRTC path, against the reference evaluator's golden outputs."""
+    torch = torch_cuda
+    g = golden("pw_piecewise_93")
+    kern = load_reference_example("piecewise").piecewise(target=TARGET)
+    b = torch.full((93,), float("nan"), device="cuda")
+    kern(to_gpu(torch, g["a"]), b)
+    assert np.array_equal(bits(b.cpu().numpy()), bits(g["b"]))
+
+    g = golden("pw_fragment_affine_257")
+    kern = load_reference_example("fragment_affine").fragment_affine(target=TARGET)
+    b = torch.full((257,), float("nan"), device="cuda")
+    kern(to_gpu(torch, g["a"]), b)
+    assert np.array_equal(bits(b.cpu().numpy()), bits(g["b"]))
+
+    g = golden("pw_window_sum_7x3x5")
+    kern = load_reference_example("window_sum").window_sum(target=TARGET)
+    a = to_gpu(torch, g["a"])
+    for (rows, cols), expect in zip(g["windows"], g["b"]):
+        b = torch.full((7,), float("nan"), device="cuda")
+        kern(a, b, int(rows), int(cols))
+        assert np.array_equal(bits(b.cpu().numpy()), bits(expect)), (rows, cols)
