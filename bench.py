@@ -1218,12 +1218,15 @@ def run_reference(args, ops):
         if name == HEADLINE:
             head = (op, v, cb)
     op, v, cb = head
+    # one step = one whole BASELINE workload, at the rate the bounded sample measured
+    ms = round(op.total_units() / (v * op.per_unit()) * 1e3, 6) if v > 0 else None
     line = {
         "impl": "reference", "metric": BASELINE_METRIC, "value": round(v, 4), "unit": op.unit, "n_gpus": args.gpus,
-        "steps": steps, "warmup": args.warmup, "ms_per_step": None, "higher_is_better": True, "scaling": "strong",
+        "steps": steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded, BASELINE.json distributions)",
-        "config": {"workload": op.config, "op": op.name, "path": "CPU oracle port of the reference algorithm",
-                   "torch": torch.__version__},
+        "config": {"workload": op.config, "op": op.name,
+                   "path": "CPU oracle port of the reference algorithm; ms_per_step = one whole workload at the "
+                           "sampled rate", "torch": torch.__version__},
         "cpu_baseline": cb, "e2e": {"value": round(v, 4), "unit": op.unit, "h2d_bytes_per_step": 0,
                                     "d2h_bytes_per_step": 0},
         "ops": per,
