@@ -141,13 +141,24 @@ int ntl_gemm_f16_f32_noalloc(const uint16_t* a, const uint16_t* b, float* c, con
 /* FlashAttention-2 forward, fp16 Q,K,V,O [batch, heads, seq, dim] row-major.
  *   O = softmax_base2((Q K^T) * scale_log2 [causal: key <= query]) V, with P rounded to fp16
  *   before the P V product and fp32 softmax statistics.
- * Non-causal launches one CTA per (batch, head, 256-query block); causal launches a persistent
- * grid of one CTA per SM (fewer for small problems) that runs the blocks in a fixed order, so
- * kernels on other streams share SMs with it only as its CTAs finish.
+ * Non-causal launches one CTA per (batch, head, 256-query block).  Causal does the same unless
+ * the blocks, paired heaviest with lightest, fill at least 95% of whole rounds of one CTA per
+ * SM: then it launches that persistent grid, which runs the pairs in a fixed order, so kernels
+ * on other streams share SMs with it only as its CTAs finish.  Both grids give bit-identical
+ * results; ntl_fa2_set_causal_grid overrides the choice.
  * Replaces the FFI call of the kernel emitted for examples/flash_attention.py:26-79
  * (scale = log2(e)/sqrt(d) at :23, causal fill at :56-62, P cast at :74-75). */
 int ntl_fa2_fwd_f16(const uint16_t* q, const uint16_t* k, const uint16_t* v, uint16_t* o, int64_t batch,
                     int64_t heads, int64_t seq, int64_t dim, float scale_log2, int causal, ntl_stream_t stream);
+
+/* Grid of the causal ntl_fa2_fwd_f16 calls this process makes from now on: NTL_FA2_GRID_AUTO
+ * (the rule above, the default), NTL_FA2_GRID_PERSISTENT or NTL_FA2_GRID_PER_BLOCK.
+ * Process-wide, like ntl_set_wait_limit; NTL_ERR_INVALID for any other value.  No reference
+ * counterpart. */
+#define NTL_FA2_GRID_AUTO 0
+#define NTL_FA2_GRID_PERSISTENT 1
+#define NTL_FA2_GRID_PER_BLOCK 2
+int ntl_fa2_set_causal_grid(int mode);
 
 /* Generic elementwise programs (outside the families above): run-time compiled kernels.
  * ntl_rtc_build compiles CUDA C `source` (one extern "C" __global__ function named

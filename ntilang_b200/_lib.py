@@ -50,6 +50,7 @@ SIGNATURES = {
     "ntl_device_status": (ctypes.c_int, [ctypes.POINTER(ctypes.c_uint32)]),
     "ntl_clear_device_status": (ctypes.c_int, []),
     "ntl_set_wait_limit": (ctypes.c_int, [c_i64]),
+    "ntl_fa2_set_causal_grid": (ctypes.c_int, [ctypes.c_int]),
     "ntl_launch_count": (ctypes.c_int64, []),
 }
 
@@ -107,6 +108,14 @@ def clear_device_status() -> None:
 
 def set_wait_limit(polls: int) -> None:
     call("ntl_set_wait_limit", int(polls))
+
+
+FA2_GRID_AUTO, FA2_GRID_PERSISTENT, FA2_GRID_PER_BLOCK = 0, 1, 2
+
+
+def set_fa2_causal_grid(mode: int) -> None:
+    """Grid of later causal attention launches: FA2_GRID_AUTO (default), _PERSISTENT or _PER_BLOCK."""
+    call("ntl_fa2_set_causal_grid", int(mode))
 
 
 def gemm_workspace_size(M, N, K, b_trans) -> int:

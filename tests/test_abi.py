@@ -49,6 +49,9 @@ def test_host_side_validation_without_gpu(built_library):
     assert h.ntl_gemm_f16_f32(16, 16, 16, None, 1, 1.0, 0, 8, 8, 8, 0, None) == 1
     assert h.ntl_softmax_f32(16, 32, 4, 1 << 20, None) == 2
     assert h.ntl_set_wait_limit(0) == 1
+    assert h.ntl_fa2_set_causal_grid(3) == 1 and b"causal grid" in h.ntl_last_error()
+    for mode in (_lib.FA2_GRID_PERSISTENT, _lib.FA2_GRID_PER_BLOCK, _lib.FA2_GRID_AUTO):
+        assert h.ntl_fa2_set_causal_grid(mode) == 0
     # empty problems are no-ops that succeed without touching the device
     assert h.ntl_vadd_f32(None, None, None, 0, None) == 0
     assert h.ntl_rmsnorm_f32(None, None, None, 0, 128, 1e-6, 1 / 128, None) == 0

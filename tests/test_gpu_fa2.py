@@ -155,17 +155,29 @@ def test_fa2_timeout_path_reports_error(torch_cuda, causal):
     torch.testing.assert_close(out.float(), sdpa_fp32(torch, q, k, v, causal), rtol=0, atol=ATOL)
 
 
-@pytest.mark.parametrize("b,h,s", [(3, 5, 600), (1, 1, 100), (2, 3, 4096), (64, 16, 512)])
-def test_fa2_causal_persistent_unit_counts(torch_cuda, b, h, s):
-    """Causal attention runs on the persistent grid: an odd number of units (the last pair has one)
-    with a dead second query tile in the last query block (S = 600, 100), fewer pairs of units than
-    SMs, and several pairs per CTA; sampled heads against fp32 attention."""
+@pytest.mark.parametrize("b,h,s", [(3, 5, 600), (1, 1, 100), (2, 3, 4096), (64, 16, 512), (2, 32, 4096)])
+def test_fa2_causal_grids_agree(torch_cuda, b, h, s):
+    """Causal attention on each grid, pinned with ntl_fa2_set_causal_grid, and on the automatic
+    choice: the persistent grid with an odd number of units (the last pair has one), a dead second
+    query tile in the last query block (S = 600, 100), fewer pairs of units than SMs and several
+    pairs per CTA; the one-CTA-per-block grid on the same shapes.  All three are bit-identical, and
+    sampled heads match fp32 attention."""
+    from ntilang_b200 import _lib
+
     torch = torch_cuda
     d = 128
     g = torch.Generator(device="cuda").manual_seed(b * 1000 + h * 10 + s)
     q, k, v = (torch.randn(b, h, s, d, device="cuda", generator=g, dtype=torch.float16) for _ in range(3))
-    out = K.flash_attention(b, h, s, d, True)(q, k, v)
-    torch.cuda.synchronize()
+    outs = {}
+    try:
+        for mode in (_lib.FA2_GRID_PERSISTENT, _lib.FA2_GRID_PER_BLOCK, _lib.FA2_GRID_AUTO):
+            _lib.set_fa2_causal_grid(mode)
+            outs[mode] = K.flash_attention(b, h, s, d, True)(q, k, v)
+            torch.cuda.synchronize()
+    finally:
+        _lib.set_fa2_causal_grid(_lib.FA2_GRID_AUTO)
+    out = outs[_lib.FA2_GRID_PERSISTENT]
+    assert torch.equal(outs[_lib.FA2_GRID_PER_BLOCK], out) and torch.equal(outs[_lib.FA2_GRID_AUTO], out)
     for bb, hh in {(0, 0), (b - 1, h - 1), (b // 2, h // 2)}:
         ref = sdpa_fp32(torch, q[bb:bb + 1, hh:hh + 1], k[bb:bb + 1, hh:hh + 1], v[bb:bb + 1, hh:hh + 1], True)
         torch.testing.assert_close(out[bb:bb + 1, hh:hh + 1].float(), ref, rtol=0, atol=ATOL)
