@@ -261,6 +261,10 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_tc_kernel(const __grid_consta
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = ctl->tmem_base;
+  // Launched with programmatic stream serialization (no workspace): the setup above overlaps
+  // the previous kernel on the stream; every global access (A, B, bias, C) comes after this.
+  pdl_wait();
+  pdl_trigger();
 
   if (warp == 0) {
     // ------------------------------------------------------------ TMA producer
@@ -638,6 +642,10 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_pair_kernel(const __grid_cons
   cluster_sync_all();
   tc_fence_after();
   const uint32_t tmem_base = ctl->tmem_base;
+  // Launched with programmatic stream serialization (no workspace): the setup above overlaps
+  // the previous kernel on the stream; every global access (A, B, bias, C) comes after this.
+  pdl_wait();
+  pdl_trigger();
 
   if (warp == 0) {
     // ------------------------------------------------------------ TMA producer (both CTAs)
@@ -1087,11 +1095,16 @@ int gemm_pair_launch(const uint16_t* a, const uint16_t* b, GemmParams p, void* w
   cfg.blockDim = dim3(THREADS, 1, 1);
   cfg.dynamicSmemBytes = PR_SMEM_BYTES;
   cfg.stream = s;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = 2, attr[0].val.clusterDim.y = 1, attr[0].val.clusterDim.z = 1;
+  // Without a workspace the kernel's setup may overlap the previous kernel (it waits with
+  // pdl_wait before touching global memory); with one, the launch keeps plain stream order
+  // behind whatever cleared the workspace's flags.
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = pl.split > 1 ? 1 : 2;
   cudaError_t e = cudaLaunchKernelEx(&cfg, gemm_pair_kernel, ma, mb, p);
   ntl_note_launch();
   if (e != cudaSuccess) return ntl_fail(NTL_ERR_CUDA, "gemm (CTA-pair path) launch: %s", cudaGetErrorString(e));
@@ -1187,7 +1200,16 @@ int gemm_launch(const uint16_t* a, const uint16_t* b, float* c, const float* bia
     if (int rc = make_map_f16(&mb, b, K, N, 64, BK)) return rc;
   }
   if (int rc = ensure_smem_attr()) return rc;
-  gemm_tc_kernel<<<pl.grid, THREADS, SMEM_BYTES, s>>>(ma, mb, p);
+  if (pl.sk_ctas > 0) {
+    gemm_tc_kernel<<<pl.grid, THREADS, SMEM_BYTES, s>>>(ma, mb, p);
+  } else {
+    // No workspace: the setup may overlap the previous kernel (see the pair launch).
+    cudaError_t e = ntl_launch_pdl(gemm_tc_kernel, dim3(pl.grid), dim3(THREADS), SMEM_BYTES, s, ma, mb, p);
+    if (e != cudaSuccess) {
+      ntl_note_launch();
+      return ntl_fail(NTL_ERR_CUDA, "gemm (tcgen05 path) launch: %s", cudaGetErrorString(e));
+    }
+  }
   ntl_note_launch();
   return ntl_check_launch("gemm (tcgen05 path) launch");
 }

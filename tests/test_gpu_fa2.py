@@ -129,18 +129,21 @@ def test_fa2_baseline_size_every_head(torch_cuda, causal):
     assert worst <= ATOL, worst
 
 
-@pytest.mark.parametrize("causal", [False, True])
-def test_fa2_timeout_path_reports_error(torch_cuda, causal):
+@pytest.mark.parametrize("causal,grid", [(False, "auto"), (True, "persistent"), (True, "per_block")])
+def test_fa2_timeout_path_reports_error(torch_cuda, causal, grid):
     """A 1-poll wait limit makes the bounded waits give up, in the one-CTA-per-unit kernel
-    (non-causal) and the persistent one (causal, several units per CTA): the launch must return,
-    report a status and leave the context usable."""
+    (non-causal, and causal pinned to that grid) and the persistent one (causal pinned to it, two
+    units per CTA): the launch must return, report a status and leave the context usable."""
     torch = torch_cuda
     from ntilang_b200 import _lib
 
+    mode = {"auto": _lib.FA2_GRID_AUTO, "persistent": _lib.FA2_GRID_PERSISTENT,
+            "per_block": _lib.FA2_GRID_PER_BLOCK}[grid]
     b, h, s, d = (1, 2, 512, 128) if not causal else (2, 8, 1024, 128)
     q, k, v = (torch.randn(b, h, s, d, device="cuda", dtype=torch.float16) for _ in range(3))
     o = torch.empty_like(q)
     _lib.clear_device_status()
+    _lib.set_fa2_causal_grid(mode)
     _lib.set_wait_limit(1)
     try:
         _lib.call("ntl_fa2_fwd_f16", q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), b, h, s, d,
@@ -149,6 +152,7 @@ def test_fa2_timeout_path_reports_error(torch_cuda, causal):
         status = _lib.device_status()
     finally:
         _lib.set_wait_limit(1 << 26)
+        _lib.set_fa2_causal_grid(_lib.FA2_GRID_AUTO)
         _lib.clear_device_status()
     assert status != 0
     out = K.flash_attention(b, h, s, d, causal)(q, k, v)

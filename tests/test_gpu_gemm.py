@@ -258,3 +258,32 @@ def test_gemm_n_split_tail_tiles(torch_cuda, m, n, k, trans_b, bias_mode):
         _lib.call("ntl_gemm_f16_f32", a.data_ptr(), b.data_ptr(), c.data_ptr(), bias.data_ptr(), bias_mode, 0.75, 1,
                   m, n, k, trans_b, torch.cuda.current_stream().cuda_stream)
         check(torch, c, ref)
+
+
+@pytest.mark.parametrize("m,n,k", [(1024, 1024, 1024), (512, 4096, 1024), (96, 512, 256)])
+def test_gemm_dependent_launches_in_one_stream(torch_cuda, m, n, k):
+    """The tcgen05 GEMMs start their setup while the previous kernel on the stream runs, and
+    touch global memory only after it completes.  Twenty rounds, with no synchronisation, of
+    C = A B; D = C + E (a vector add, which also overlaps its predecessor); C = A2 B2: every D is
+    exactly A B + E, so no GEMM wrote C while the add still read it, and no add read C before the
+    GEMM finished writing it."""
+    torch = torch_cuda
+    g = torch.Generator(device="cuda").manual_seed(m + n + k)
+    a, a2 = ((torch.randn(m, k, device="cuda", generator=g) / k ** 0.5).half() for _ in range(2))
+    b, b2 = ((torch.randn(k, n, device="cuda", generator=g) / k ** 0.5).half() for _ in range(2))
+    e = torch.randn(m * n, device="cuda", generator=g)
+    gemm = K.matmul(m, n, k)
+    add = K.vector_add(m * n)
+    want = gemm(a, b).view(-1) + e
+    assert not torch.equal(gemm(a2, b2).view(-1) + e, want)
+    c = torch.empty(m, n, device="cuda")
+    outs = []
+    for _ in range(20):
+        gemm(a, b, c)
+        d = torch.empty(m * n, device="cuda")
+        add(c.view(-1), e, d)
+        gemm(a2, b2, c)
+        outs.append(d)
+    torch.cuda.synchronize()
+    for d in outs:
+        assert torch.equal(d, want)
